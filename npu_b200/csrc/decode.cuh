@@ -1,0 +1,26 @@
+// Parameters and launcher of the split-KV decode kernels (decode.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace b2a {
+
+struct DecodeParams {
+  const __nv_bfloat16* q;  // [B, Hq, D]
+  long long q_sb, q_sh;
+  const int* seqlens;      // [B], device
+  float* part_o;           // [B, Hkv, max_splits, group, D]
+  float* part_lse;         // [B, Hkv, max_splits, group]
+  void* o;                 // [B, Hq, D]
+  long long o_sb, o_sh;
+  int B, Hq, Hkv, Lmax, group, split_len, max_splits;
+  float scale_log2;
+  int out_fp32;
+  int* err;
+};
+
+// Launch the split kernel and the LSE combine on `st`. Returns 0 on success,
+// -3 for an unsupported head_dim, another negative value on launch failure.
+int launch_decode(int D, const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p, cudaStream_t st);
+
+}  // namespace b2a

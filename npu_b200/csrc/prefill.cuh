@@ -1,0 +1,87 @@
+// Causal GQA prefill attention for sm_100a (tcgen05 + TMEM + TMA).
+//
+// Semantics follow the reference's FlashAttention-2 forward
+// (npu/fa_ref.py:42-131, flash_attention_ref): for query row r with absolute
+// position start_pos + r and key column c, the key is masked iff
+// c > start_pos + r (causal); rows with no unmasked key produce 0
+// (npu/fa_ref.py:112-128); the softmax scale is a runtime argument (the
+// reference kernel hard-codes 1/sqrt(64), npu/fa_kernel.cc:37-38). Query head h
+// reads key/value head h / (Hq / Hkv), the repeat_interleave mapping of
+// smollm.py:205-207, without materialising the expanded K/V.
+//
+// One CTA owns a 256-row query block of one (batch, query head): two 128-row
+// tiles that ping-pong on the tensor core, so one tile's softmax overlaps the
+// other tile's MMAs. Warp roles (12 warps):
+//   warp 0      TMA producer: Q once, then K_j / V_j tiles through a ring
+//   warp 1      TMEM owner + single-thread UMMA issuer
+//   warps 2-3   idle (keep the softmax warpgroups warpgroup-aligned)
+//   warps 4-7   softmax + epilogue for tile 0 (thread = row = TMEM lane)
+//   warps 8-11  softmax + epilogue for tile 1
+// TMEM (512 columns): S_0, S_1 (128 fp32 columns each), O_0, O_1 (D columns).
+// P (bf16) goes through shared memory in the 128B-swizzled K-major layout
+// that the PV UMMA reads as its A operand.
+#pragma once
+
+#include "common.cuh"
+
+namespace b2a {
+
+struct PrefillParams {
+  void* o;             // [B, Hq, Tq, D], innermost stride 1
+  long long o_sb, o_sh, o_st;  // element strides
+  float* lse;          // optional [B, Hq, Tq] natural-log LSE (nullptr = skip)
+  const int* start_pos_arr;  // optional per-batch start position (device)
+  int start_pos;
+  int B, Hq, Hkv, Tq, Tk;
+  float scale_log2;    // softmax scale * log2(e)
+  int causal;
+  int out_fp32;
+  int n_qblk;          // ceil(Tq / 256)
+  int* err;            // device error word (may be nullptr)
+};
+
+template <int D>
+struct PrefillCfg {
+  static constexpr int BM = 128;  // rows per Q tile == TMEM lanes
+  static constexpr int BN = 128;  // keys per K/V tile
+  static constexpr int NQT = 2;   // Q tiles per CTA
+  static constexpr int KCH = D / 64;  // 128-byte swizzle chunks per row
+  static constexpr int CHUNK_BYTES = 128 * 128;  // 128 rows x 128 B
+  static constexpr int Q_TILE_BYTES = BM * D * 2;
+  static constexpr int KV_TILE_BYTES = BN * D * 2;
+  static constexpr int P_TILE_BYTES = BM * BN * 2;
+  static constexpr int STAGES = (D == 64) ? 6 : 3;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_KV = OFF_Q + NQT * Q_TILE_BYTES;
+  static constexpr int OFF_P = OFF_KV + STAGES * KV_TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_P + NQT * P_TILE_BYTES;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int S_COL = 0;          // S_t at S_COL + t * BN
+  static constexpr int O_COL = NQT * BN;   // O_t at O_COL + t * D
+  static constexpr int THREADS = 384;
+  static_assert(D == 64 || D == 128, "two-tile prefill supports head_dim 64 and 128");
+  static_assert(O_COL + NQT * D <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+// Barrier slots inside the OFF_BAR region.
+struct PrefillBars {
+  uint64_t q_full;
+  uint64_t kv_full[8];
+  uint64_t kv_empty[8];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_full[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// Launch the prefill kernel on `st`. Returns 0 on success, -3 for an
+// unsupported head_dim, another negative value on launch failure.
+int launch_prefill(int D, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                   const PrefillParams& p, cudaStream_t st);
+
+}  // namespace b2a

@@ -1,0 +1,97 @@
+"""Drop-in replacement for the reference's NpuAttention (npu/fa.py:167-332).
+
+`smollm.py` reaches attention through an object stored in
+`layer.npu["attention"]` (smollm.py:141,163,316-320). It reads `.BR`/`.BC`,
+pads T and Tk to those multiples, flattens (batch, head, query block) into N
+and calls `run_batch(Q_stack, K_stack, V_stack, start_rows, causal)`
+(smollm.py:129-166). This class keeps that contract — same attribute names,
+argument meaning, preconditions (npu/fa.py:220-223) and bf16 result — and runs
+every block on the sm_100a prefill kernel. Block n is an independent problem
+whose query row r sits at absolute position start_rows[n] + r; there is no
+per-dispatch static state and no xclbin cache to key.
+"""
+from __future__ import annotations
+
+from typing import Optional, Sequence
+
+import torch
+
+from . import api
+
+
+class NpuAttention:
+    """Runs FlashAttention on a batch of query blocks in one kernel launch.
+
+    BR/BC default to 128 (the kernel's tile); any BR works, BC is only the
+    padding granularity the caller uses for Tk (the reference asserts
+    TK % BC == 0, npu/fa.py:222). `n_cores` is accepted for signature
+    compatibility and ignored: the grid covers all 148 SMs.
+    """
+
+    def __init__(self, BR: int = 128, BC: int = 128, D: int = 64, n_cores: Optional[int] = None,
+                 device: Optional[torch.device] = None, out_dtype: torch.dtype = torch.bfloat16):
+        if D not in (64, 128):
+            raise ValueError(f"head_dim {D} not supported by the prefill kernel (64, 128)")
+        self.BR, self.BC, self.D = BR, BC, D
+        self.n_cores = n_cores
+        self.device = torch.device(device) if device is not None else None
+        self.out_dtype = out_dtype
+
+    def _dev(self, t: torch.Tensor) -> torch.device:
+        if t.is_cuda:
+            return t.device
+        if self.device is not None:
+            return self.device
+        if not torch.cuda.is_available():
+            raise RuntimeError("NpuAttention needs a CUDA device (no CPU path)")
+        return torch.device("cuda", torch.cuda.current_device())
+
+    def run_batch(
+        self,
+        Q_stack: torch.Tensor,  # [N, BR, D]
+        K_stack: torch.Tensor,  # [N, TK, D]
+        V_stack: torch.Tensor,  # [N, TK, D]
+        start_rows: Sequence[int],  # length N
+        causal: bool = True,
+    ) -> torch.Tensor:
+        """Return O_stack [N, BR, D] (bf16 unless out_dtype says otherwise).
+
+        Inputs may live on the host (as in the reference, whose model runs on
+        the CPU) or on the GPU; the result comes back on the inputs' device.
+        """
+        N_in, BR, D = Q_stack.shape
+        TK = K_stack.shape[1]
+        assert (BR, D) == (self.BR, self.D)
+        assert K_stack.shape == (N_in, TK, D) and V_stack.shape == (N_in, TK, D)
+        assert TK % self.BC == 0
+        assert len(start_rows) == N_in
+        home = Q_stack.device
+        dev = self._dev(Q_stack)
+        q = Q_stack.to(device=dev, dtype=torch.bfloat16, non_blocking=True).unsqueeze(1)
+        k = K_stack.to(device=dev, dtype=torch.bfloat16, non_blocking=True).unsqueeze(1)
+        v = V_stack.to(device=dev, dtype=torch.bfloat16, non_blocking=True).unsqueeze(1)
+        sp = torch.as_tensor(list(start_rows), dtype=torch.int32).to(dev, non_blocking=True)
+        o = api.prefill(q.contiguous(), k.contiguous(), v.contiguous(), start_pos_per_batch=sp,
+                        causal=causal, out_dtype=self.out_dtype)
+        o = o.squeeze(1)
+        return o if home == o.device else o.to(home)
+
+    def run_one(self, Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,
+                start_row: int = 0, causal: bool = False) -> torch.Tensor:
+        """Single-Q-block wrapper around run_batch (npu/fa.py:325-332)."""
+        O = self.run_batch(Q.unsqueeze(0), K.unsqueeze(0), V.unsqueeze(0), [start_row], causal=causal)
+        return O.squeeze(0)
+
+
+def enable_attention(model, decode_attention: bool = False, **kw) -> NpuAttention:
+    """Route every layer's attention of a smollm.py `SmolLM` through the B200
+    kernel, the `attention=True` branch of SmolLM.enable_npu
+    (smollm.py:267-320) with projections left on their current device.
+    Returns the shared NpuAttention."""
+    shared = NpuAttention(D=model.cfg.head_dim, **kw)
+    for layer in model.layers:
+        layer.npu = {"attention": shared}
+        layer.npu_decode = {}
+        layer.npu_decode_cpu = False
+        layer.npu_decode_attention = decode_attention
+    return shared

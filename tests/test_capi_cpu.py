@@ -1,0 +1,129 @@
+"""The C-ABI library without a GPU: it loads, exports every declared symbol,
+and rejects bad arguments before touching CUDA. No compute is launched."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from npu_b200 import _lib
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+FAKE = 0x10000  # 16-byte aligned, never dereferenced: validation fails first
+
+
+def declared_symbols():
+    names = set()
+    for h in HEADERS:
+        names |= set(re.findall(r"B2A_API\s+[\w\s\*]+?\b(b2a_\w+)\s*\(", h.read_text()))
+    return sorted(names)
+
+
+def test_headers_declare_the_abi():
+    names = declared_symbols()
+    for want in ("b2a_prefill", "b2a_decode", "b2a_decode_workspace_bytes", "b2a_strerror",
+                 "b2a_get_device_error", "b2a_decode_default_split", "b2a_version"):
+        assert want in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert set(declared_symbols()) <= set(_lib.SIGNATURES)
+
+
+def test_strerror_and_version():
+    lib = _lib.load()
+    for code in range(0, -12, -1):
+        text = lib.b2a_strerror(code).decode()
+        assert text and "unknown" not in text
+    assert "unknown" in lib.b2a_strerror(-99).decode()
+    assert lib.b2a_version() >= 100
+
+
+def _prefill(**over):
+    args = dict(q=FAKE, k=FAKE, v=FAKE, o=FAKE, lse=None, B=1, Hq=8, Hkv=2, Tq=64, Tk=64, D=128,
+                qs=(8 * 64 * 128, 64 * 128, 128), ks=(2 * 64 * 128, 64 * 128, 128),
+                vs=(2 * 64 * 128, 64 * 128, 128), os=(8 * 64 * 128, 64 * 128, 128),
+                sp=0, spb=None, scale=0.125, causal=1, fp32=1)
+    args.update(over)
+    a = args
+    return _lib.load().b2a_prefill(a["q"], a["k"], a["v"], a["o"], a["lse"], a["B"], a["Hq"], a["Hkv"], a["Tq"],
+                                   a["Tk"], a["D"], _lib.ll3(*a["qs"]), _lib.ll3(*a["ks"]), _lib.ll3(*a["vs"]),
+                                   _lib.ll3(*a["os"]), a["sp"], a["spb"], a["scale"], a["causal"], a["fp32"],
+                                   None)
+
+
+def test_prefill_argument_validation():
+    assert _prefill(q=None) == _lib.B2A_ERR_INVALID_ARG
+    assert _prefill(B=0) == _lib.B2A_ERR_INVALID_ARG
+    assert _prefill(Tq=0) == _lib.B2A_ERR_INVALID_ARG
+    assert _prefill(scale=0.0) == _lib.B2A_ERR_INVALID_ARG
+    assert _prefill(scale=float("nan")) == _lib.B2A_ERR_INVALID_ARG
+    assert _prefill(D=96) == _lib.B2A_ERR_HEAD_DIM
+    assert _prefill(D=256) == _lib.B2A_ERR_HEAD_DIM
+    assert _prefill(Hkv=3) == _lib.B2A_ERR_GQA
+    assert _prefill(q=FAKE + 2) == _lib.B2A_ERR_ALIGNMENT
+    assert _prefill(qs=(8 * 64 * 128, 64 * 128, 100)) == _lib.B2A_ERR_ALIGNMENT
+    assert _prefill(lse=FAKE + 2) == _lib.B2A_ERR_ALIGNMENT
+
+
+def test_prefill_valid_args_without_gpu_report_cuda_error():
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present; covered by the gpu tests")
+    assert _prefill() in (_lib.B2A_ERR_CUDA, _lib.B2A_ERR_DEVICE)
+
+
+def test_decode_workspace_arithmetic():
+    lib = _lib.load()
+    # B=128, Hq=32, Hkv=4, D=128, Lmax=32768, split 2048 -> 16 splits, group 8
+    n = 128 * 4 * 16 * 8
+    want = ((n * 128 * 4 + 255) // 256) * 256 + ((n * 4 + 255) // 256) * 256
+    assert lib.b2a_decode_workspace_bytes(128, 32, 4, 128, 32768, 2048) == want
+    assert lib.b2a_decode_workspace_bytes(128, 32, 4, 128, 32768, 100) == 0  # not a multiple of 64
+    assert lib.b2a_decode_workspace_bytes(1, 32, 1, 128, 64, 64) == 0       # group 32 > 16
+    assert lib.b2a_decode_workspace_bytes(1, 8, 2, 96, 64, 64) == 0         # head_dim
+    s = lib.b2a_decode_default_split(128, 4, 32768)
+    assert s % 64 == 0 and 512 <= s <= 4096
+    assert lib.b2a_decode_default_split(1, 1, 100) == 512
+
+
+def test_decode_argument_validation():
+    lib = _lib.load()
+
+    def call(**over):
+        a = dict(q=FAKE, k=FAKE, v=FAKE, sl=FAKE, o=FAKE, B=2, Hq=8, Hkv=2, L=256, D=128, split=64,
+                 ws=FAKE, wsb=1 << 30, scale=0.1)
+        a.update(over)
+        return lib.b2a_decode(a["q"], a["k"], a["v"], a["sl"], a["o"], a["B"], a["Hq"], a["Hkv"], a["L"], a["D"],
+                              _lib.ll2(8 * 128, 128), _lib.ll3(2 * 256 * 128, 256 * 128, 128),
+                              _lib.ll3(2 * 256 * 128, 256 * 128, 128), _lib.ll2(8 * 128, 128),
+                              a["scale"], a["split"], 1, a["ws"], a["wsb"], None)
+
+    assert call(sl=None) == _lib.B2A_ERR_INVALID_ARG
+    assert call(D=80) == _lib.B2A_ERR_HEAD_DIM
+    assert call(Hkv=3) == _lib.B2A_ERR_GQA
+    assert call(split=100) == _lib.B2A_ERR_INVALID_ARG
+    assert call(k=FAKE + 8) == _lib.B2A_ERR_ALIGNMENT
+    assert call(ws=None) == _lib.B2A_ERR_WORKSPACE
+    assert call(wsb=16) == _lib.B2A_ERR_WORKSPACE
+    if not torch.cuda.is_available():
+        assert call() in (_lib.B2A_ERR_CUDA, _lib.B2A_ERR_DEVICE)
+
+
+def test_python_api_refuses_cpu_tensors():
+    from npu_b200 import api
+
+    q = torch.zeros(1, 2, 8, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        api.prefill(q, q, q)
+    with pytest.raises(ValueError, match="CUDA"):
+        api.decode(q[:, :, 0], q, q, torch.zeros(1, dtype=torch.int32))
+
+
+def test_b2a_error_carries_status_text():
+    err = _lib.B2AError(_lib.B2A_ERR_GQA, "b2a_prefill")
+    assert err.code == _lib.B2A_ERR_GQA and "multiple" in str(err)

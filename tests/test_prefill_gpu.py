@@ -1,0 +1,199 @@
+"""Parity of the sm_100a prefill kernel with the fp32 oracle (max|Δ| <= 2e-2,
+the north-star tolerance), through the C ABI via npu_b200.api / NpuAttention."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import from_bits
+from oracle import attention as A
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _rand(shape, gen, dev):
+    return torch.randn(*shape, generator=gen).to(torch.bfloat16).to(dev)
+
+
+def test_umma_layouts(cuda_dev):
+    """One 128^3 tcgen05 MMA per operand layout (K-major B and MN-major B)."""
+    from npu_b200 import _lib
+
+    g = torch.Generator().manual_seed(0)
+    a = torch.randn(128, 128, generator=g).bfloat16()
+    b = torch.randn(128, 128, generator=g).bfloat16()
+    for mn in (0, 1):
+        c = torch.zeros(128, 128, dtype=torch.float32, device=cuda_dev)
+        ad, bd = a.to(cuda_dev), b.to(cuda_dev)
+        rc = _lib.load().b2a_diag_umma_gemm(ad.data_ptr(), bd.data_ptr(), c.data_ptr(), mn,
+                                            torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+        torch.cuda.synchronize()
+        ref = a.float() @ (b.float() if mn else b.float().T)
+        assert (c.cpu() - ref).abs().max().item() < 1e-2, f"b_mn_major={mn}"
+
+
+@pytest.mark.parametrize("i", range(5))
+def test_reference_selftest_grid(cuda_dev, fa_golden, i):
+    """The reference's own self-test shapes (npu/fa_ref.py:148-167)."""
+    from npu_b200 import api
+
+    g = fa_golden
+    q, k, v = (from_bits(g[f"selftest{i}_{n}"]).to(cuda_dev) for n in "qkv")
+    sp = int(g[f"selftest{i}_meta"][3])
+    out = api.prefill(q, k, v, start_pos=sp, causal=True)
+    ref = g[f"selftest{i}_fa_32_32"]
+    assert np.abs(out.cpu().numpy() - ref).max() <= TOL
+
+
+def test_config1_gqa(cuda_dev, fa_golden):
+    """Config 1: B=1, T=128, 9/3 heads, D=64, fp32 out vs the reference's
+    torch fp32 attention (golden)."""
+    from npu_b200 import api
+
+    g = fa_golden
+    q, k, v = (from_bits(g[f"cfg1_{n}"]).to(cuda_dev) for n in "qkv")
+    out = api.prefill(q, k, v, scale=1.0 / 8)
+    assert np.abs(out.cpu().numpy() - g["cfg1_dense"]).max() <= TOL
+
+
+def test_chunked_prefill_golden(cuda_dev, fa_golden):
+    from npu_b200 import api
+
+    g = fa_golden
+    q, k, v = (from_bits(g[f"chunk_{n}"]).to(cuda_dev) for n in "qkv")
+    assert np.abs(api.prefill(q, k, v, start_pos=80).cpu().numpy() - g["chunk_fa_16_32"]).max() <= TOL
+    out = api.prefill(q, k, v, causal=False).cpu().numpy()
+    assert np.abs(out - g["chunk_nomask_fa_32_32"]).max() <= TOL
+
+
+CASES = [
+    # B, Hq, Hkv, Tq, Tk, D, start_pos, causal
+    (1, 1, 1, 1, 1, 64, 0, True),
+    (1, 2, 1, 17, 17, 64, 0, True),
+    (2, 4, 2, 127, 127, 128, 0, True),
+    (1, 4, 4, 128, 128, 128, 0, True),
+    (1, 2, 1, 129, 129, 64, 0, True),
+    (1, 2, 2, 255, 300, 128, 45, True),
+    (2, 8, 1, 256, 256, 64, 0, True),
+    (1, 8, 2, 257, 257, 128, 0, True),
+    (1, 3, 1, 300, 1000, 64, 700, True),
+    (2, 4, 4, 200, 333, 128, 0, False),
+    (1, 2, 1, 1000, 1000, 128, 0, True),
+    (1, 32, 4, 512, 512, 128, 0, True),
+]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Tq,Tk,D,sp,causal", CASES)
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_prefill_matches_oracle(cuda_dev, B, Hq, Hkv, Tq, Tk, D, sp, causal, out_dtype):
+    from npu_b200 import api
+
+    g = torch.Generator().manual_seed(B * 1000 + Tq * 7 + Tk + D)
+    q, k, v = _rand((B, Hq, Tq, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev)
+    out = api.prefill(q, k, v, start_pos=sp, causal=causal, out_dtype=out_dtype)
+    ref = A.dense_attention(q.cpu(), k.cpu(), v.cpu(), start_pos=sp, causal=causal)
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err <= TOL, err
+    assert torch.isfinite(out).all()
+
+
+def test_strided_bthd_inputs(cuda_dev):
+    """q/k/v as [B, T, H, D] buffers viewed as [B, H, T, D] (the layout the
+    projections produce before transpose(1, 2), smollm.py:195-197)."""
+    from npu_b200 import api
+
+    g = torch.Generator().manual_seed(5)
+    B, T, Hq, Hkv, D = 2, 300, 8, 2, 64
+    qb = _rand((B, T, Hq, D), g, cuda_dev)
+    kb = _rand((B, T, Hkv, D), g, cuda_dev)
+    vb = _rand((B, T, Hkv, D), g, cuda_dev)
+    q, k, v = qb.transpose(1, 2), kb.transpose(1, 2), vb.transpose(1, 2)
+    out = api.prefill(q, k, v)
+    ref = A.dense_attention(q.cpu(), k.cpu(), v.cpu())
+    assert (out.cpu() - ref).abs().max().item() <= TOL
+
+
+def test_fully_masked_rows_and_empty_keys(cuda_dev):
+    from npu_b200 import api
+
+    g = torch.Generator().manual_seed(6)
+    q = _rand((1, 2, 64, 64), g, cuda_dev)
+    k = _rand((1, 2, 64, 64), g, cuda_dev)
+    out = api.prefill(q, k, k, start_pos=-10)
+    ref = A.dense_attention(q.cpu(), k.cpu(), k.cpu(), start_pos=-10)
+    assert torch.all(out[:, :, :10] == 0)
+    assert (out.cpu() - ref).abs().max().item() <= TOL
+    out = api.prefill(q, k, k, start_pos=-1_000_000)
+    assert torch.all(out == 0)
+    empty = k[:, :, :0]
+    out = api.prefill(q, empty, empty)
+    assert torch.all(out == 0)
+
+
+def test_per_batch_start_positions_and_lse(cuda_dev):
+    from npu_b200 import api
+
+    g = torch.Generator().manual_seed(7)
+    B, Hq, Hkv, Tq, Tk, D = 3, 4, 2, 100, 400, 128
+    q, k, v = _rand((B, Hq, Tq, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev)
+    sps = [0, 150, 300]
+    out, lse = api.prefill(q, k, v, start_pos_per_batch=torch.tensor(sps, dtype=torch.int32, device=cuda_dev),
+                           return_lse=True)
+    for b, sp in enumerate(sps):
+        ref = A.dense_attention(q[b:b + 1].cpu(), k[b:b + 1].cpu(), v[b:b + 1].cpu(), start_pos=sp)
+        assert (out[b:b + 1].cpu() - ref).abs().max().item() <= TOL
+        s = (q[b].float().cpu() @ A.expand_kv(k[b:b + 1].cpu().float(), 2)[0].transpose(-1, -2)) / math.sqrt(D)
+        s = s.masked_fill(A.causal_mask(Tq, Tk, sp), float("-inf"))
+        ref_lse = torch.logsumexp(s, dim=-1)
+        assert (lse[b].cpu() - ref_lse).abs().max().item() < 1e-3
+
+
+def test_npu_attention_run_batch_contract(cuda_dev):
+    """run_batch as smollm.py:157-163 drives it: host tensors in, per-block
+    start rows, dummy blocks at -1e6 (npu/fa.py:236) -> zeros, bf16 out."""
+    from npu_b200 import NpuAttention
+
+    attn = NpuAttention(D=64)
+    g = torch.Generator().manual_seed(8)
+    N, BR, TK, D = 6, attn.BR, 256, 64
+    Q = torch.randn(N, BR, D, generator=g).bfloat16()
+    K = torch.randn(N, TK, D, generator=g).bfloat16()
+    V = torch.randn(N, TK, D, generator=g).bfloat16()
+    rows = [0, 128, 0, 128, 37, -1_000_000]
+    out = attn.run_batch(Q, K, V, rows, causal=True)
+    assert out.device.type == "cpu" and out.dtype == torch.bfloat16 and out.shape == (N, BR, D)
+    ref = A.run_batch_ref(Q, K, V, rows)
+    assert (out.float() - ref).abs().max().item() <= TOL
+    assert torch.all(out[5] == 0)
+    one = attn.run_one(Q[2], K[2], V[2], start_row=0, causal=False)
+    ref1 = A.dense_attention(Q[2][None, None], K[2][None, None], V[2][None, None], causal=False)[0, 0]
+    assert (one.float() - ref1).abs().max().item() <= TOL
+    with pytest.raises(AssertionError):
+        attn.run_batch(Q, K[:, :100], V[:, :100], rows)  # TK % BC != 0
+
+
+@pytest.mark.parametrize("T", [2048, 8192])
+def test_config3_sampled_rows(cuda_dev, T):
+    """Config 3 geometry (B=64 trimmed to 4, Hq=32, Hkv=4, D=128) at full T:
+    first, last, tile-boundary and diagonal rows against the oracle."""
+    from npu_b200 import api
+
+    g = torch.Generator().manual_seed(T)
+    B, Hq, Hkv, D = 4, 32, 4, 128
+    q, k, v = _rand((B, Hq, T, D), g, cuda_dev), _rand((B, Hkv, T, D), g, cuda_dev), _rand((B, Hkv, T, D), g, cuda_dev)
+    out = api.prefill(q, k, v, scale=1 / math.sqrt(128))
+    qc, kc, vc = q.cpu(), k.cpu(), v.cpu()
+    rows = [0, 1, 127, 128, 255, 256, T // 2, T - 129, T - 2, T - 1]
+    for b, h in [(0, 0), (1, 7), (3, 31), (2, 12)]:
+        ref = A.prefill_rows_ref(qc, kc, vc, b, h, rows)
+        assert (out[b, h, rows].cpu() - ref).abs().max().item() <= TOL
+    assert torch.isfinite(out).all()
+
+
+def test_no_device_error_left(cuda_dev):
+    from npu_b200 import api
+
+    assert api.device_error(clear=True) == 0
