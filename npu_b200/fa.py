@@ -22,13 +22,15 @@ from . import api
 class NpuAttention:
     """Runs FlashAttention on a batch of query blocks in one kernel launch.
 
-    BR/BC default to 128 (the kernel's tile); any BR works, BC is only the
+    BR defaults to 128 (the kernel's query tile); any BR works. BC is only the
     padding granularity the caller uses for Tk (the reference asserts
-    TK % BC == 0, npu/fa.py:222). `n_cores` is accepted for signature
-    compatibility and ignored: the grid covers all 148 SMs.
+    TK % BC == 0, npu/fa.py:222); it stays 32 as in the reference so the
+    decode buckets of smollm.py:20 (32, 64, ...) remain valid. `n_cores` is
+    accepted for signature compatibility and ignored: the grid covers all
+    148 SMs.
     """
 
-    def __init__(self, BR: int = 128, BC: int = 128, D: int = 64, n_cores: Optional[int] = None,
+    def __init__(self, BR: int = 128, BC: int = 32, D: int = 64, n_cores: Optional[int] = None,
                  device: Optional[torch.device] = None, out_dtype: torch.dtype = torch.bfloat16):
         if D not in (64, 128):
             raise ValueError(f"head_dim {D} not supported by the prefill kernel (64, 128)")
