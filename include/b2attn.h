@@ -117,6 +117,28 @@ B2A_API int b2a_decode(const void* q, const void* k_cache, const void* v_cache, 
                const long long* v_strides, const long long* o_strides, float scale, int split_len,
                int out_fp32, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the fixed device scratch buffer behind b2a_decode_noalloc. */
+#define B2A_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+/*
+ * b2a_decode without caller scratch, for callers that cannot allocate device
+ * memory (hosts that reserve all device memory up front and forbid later
+ * cudaMalloc/cudaFree, plugin/FFI callers holding only input and output
+ * pointers). No counterpart in the reference.
+ * Same arguments and results as b2a_decode minus the workspace. Scratch is a
+ * device array of B2A_NOALLOC_SCRATCH_BYTES inside this library, held by every
+ * GPU that loads it until exit; problems needing more return
+ * B2A_ERR_WORKSPACE (use a larger split_len, or b2a_decode). The first call on
+ * a device looks up the array's device address (cudaGetSymbolAddress): make
+ * it outside any stream capture. All calls on a device share the buffer, so
+ * calls that overlap on the GPU race; nothing in it needs to start at zero.
+ */
+B2A_API int b2a_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const int* seqlens,
+                               void* o, int B, int Hq, int Hkv, int Lmax, int D, const long long* q_strides,
+                               const long long* k_strides, const long long* v_strides,
+                               const long long* o_strides, float scale, int split_len, int out_fp32,
+                               void* stream);
+
 /*
  * Read (and optionally clear) the device error word the kernels set on the
  * current device. Synchronises `stream`. *status receives B2A_OK,
