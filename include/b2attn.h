@@ -81,7 +81,7 @@ B2A_API int b2a_version(void);
  * (npu/fa_ref.py:112-128). scale is the softmax scale (1/sqrt(D) in the
  * reference, npu/fa_ref.py:68). Tk may be 0: every row is then 0 and k / v
  * are not read (they may be NULL).
- * Supported D: 64, 128.
+ * Supported D: 64, 128, 256.
  */
 B2A_API int b2a_prefill(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv,
                 int Tq, int Tk, int D, const long long* q_strides, const long long* k_strides,

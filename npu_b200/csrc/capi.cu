@@ -153,14 +153,16 @@ int b2a_prefill(const void* q, const void* k, const void* v, void* o, float* lse
   }
   if (!q || !k || !v || !o || !qs || !ks || !vs || !os) return B2A_ERR_INVALID_ARG;
   if (!(scale > 0.f) || !std::isfinite(scale)) return B2A_ERR_INVALID_ARG;
-  if (D != 64 && D != 128) return B2A_ERR_HEAD_DIM;
+  if (D != 64 && D != 128 && D != 256) return B2A_ERR_HEAD_DIM;
   if (Hq % Hkv) return B2A_ERR_GQA;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return B2A_ERR_ALIGNMENT;
   if (lse && (reinterpret_cast<uintptr_t>(lse) & 3u)) return B2A_ERR_ALIGNMENT;
   if (!strides_ok(qs, 3, 8) || !strides_ok(ks, 3, 8) || !strides_ok(vs, 3, 8) ||
       !strides_ok(os, 3, out_fp32 ? 4 : 8))
     return B2A_ERR_ALIGNMENT;
-  const long long n_qblk = (Tq + 255) / 256;
+  // Query rows per CTA: 256 (two 128-row tiles) for D <= 128, 128 for D = 256.
+  const int rows_per_cta = D == 256 ? 128 : 256;
+  const long long n_qblk = (Tq + rows_per_cta - 1) / rows_per_cta;
   if (n_qblk * Hq * (long long)B > 0x7fffffffLL) return B2A_ERR_INVALID_ARG;
 
   int* err = nullptr;
@@ -170,8 +172,10 @@ int b2a_prefill(const void* q, const void* k, const void* v, void* o, float* lse
   CUtensorMap tq, tk, tv;
   if ((rc = tmap_bf16_4d(&tq, q, D, Tq, Hq, B, qs[2], qs[1], qs[0], 128))) return rc;
   const int kv_heads_map = Tk == 0 ? Hq : Hkv;  // Tk == 0: maps describe q, never loaded
-  if ((rc = tmap_bf16_4d(&tk, k, D, Tk, kv_heads_map, B, ks[2], ks[1], ks[0], 128))) return rc;
-  if ((rc = tmap_bf16_4d(&tv, v, D, Tk, kv_heads_map, B, vs[2], vs[1], vs[0], 128))) return rc;
+  // Key-tile rows per TMA box: 128 for the two-tile kernel, 64 for D = 256.
+  const int kv_box = D == 256 ? 64 : 128;
+  if ((rc = tmap_bf16_4d(&tk, k, D, Tk, kv_heads_map, B, ks[2], ks[1], ks[0], kv_box))) return rc;
+  if ((rc = tmap_bf16_4d(&tv, v, D, Tk, kv_heads_map, B, vs[2], vs[1], vs[0], kv_box))) return rc;
 
   b2a::PrefillParams p{};
   p.o = o;
@@ -191,7 +195,8 @@ int b2a_prefill(const void* q, const void* k, const void* v, void* o, float* lse
   p.out_fp32 = out_fp32 ? 1 : 0;
   p.n_qblk = (int)n_qblk;
   p.err = err;
-  rc = b2a::launch_prefill(D, tq, tk, tv, p, static_cast<cudaStream_t>(stream));
+  rc = D == 256 ? b2a::launch_prefill_d256(tq, tk, tv, p, static_cast<cudaStream_t>(stream))
+               : b2a::launch_prefill(D, tq, tk, tv, p, static_cast<cudaStream_t>(stream));
   if (rc == -3) return B2A_ERR_HEAD_DIM;
   return rc ? B2A_ERR_LAUNCH : B2A_OK;
 }

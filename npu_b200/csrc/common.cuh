@@ -207,6 +207,19 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Warpgroup-wide register budget change (all four warps of the warpgroup
+// execute it). The shares of all warpgroups must add up to no more than the
+// registers the CTA was launched with, or the increase waits forever: callers
+// check the kernel's launch register count on the host first.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---------------------------------------------------------------- math
 // 2^x via the MUFU ex2 instruction (approximate, flushes denormals).
 __device__ __forceinline__ float ex2(float x) {

@@ -1,10 +1,10 @@
-"""Fit the cubic used by the prefill softmax to evaluate 2^f, f in [-1/2, 1/2],
-on the FMA pipe (exp2_fma in prefill.cu).
+"""Fit the polynomials the prefill softmax uses to evaluate 2^f, f in [-1/2, 1/2],
+on the FMA pipe (exp2_fma2 in softmax.cuh): degree 3 and degree 2.
 
 Method: relative-error minimax by iteratively reweighted least squares
-(Lawson's algorithm) on a dense grid, weights 1 / 2^f. The result is printed as
-C float literals; the cubic's max relative error (~8.8e-5) is far below the
-bf16 rounding (2^-9) the P tile gets anyway.
+(Lawson's algorithm) on a dense grid, weights 1 / 2^f. The results are printed as
+C float literals with their max relative error in fp32 Horner form (cubic
+7.5e-5, quadratic 1.7e-3; the bf16 P tile itself is rounded to 2^-9).
 
     python npu_b200/csrc/exp2_poly_fit.py
 """
@@ -26,9 +26,12 @@ def fit(degree: int = 3, n: int = 20001, iters: int = 200):
 
 
 if __name__ == "__main__":
-    c, e = fit()
-    c32 = c.astype(np.float32)
-    f = np.linspace(-0.5, 0.5, 200001).astype(np.float32)
-    p = ((c32[3] * f + c32[2]) * f + c32[1]) * f + c32[0]
-    print("coefficients c0..c3:", ", ".join(f"{x:.9e}f" for x in c32))
-    print("max relative error (fp32 Horner):", float(np.max(np.abs(p / np.exp2(f.astype(np.float64)) - 1))))
+    for degree in (2, 3):
+        c, _ = fit(degree)
+        c32 = c.astype(np.float32)
+        f = np.linspace(-0.5, 0.5, 200001).astype(np.float32)
+        p = np.zeros_like(f)
+        for cc in c32[::-1]:
+            p = p * f + cc
+        err = float(np.max(np.abs(p / np.exp2(f.astype(np.float64)) - 1)))
+        print(f"degree {degree}: c0..c{degree} =", ", ".join(f"{x:.9e}f" for x in c32), f"max rel. error {err:.3e}")

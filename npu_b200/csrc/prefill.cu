@@ -2,6 +2,7 @@
 // design. The host-side launcher (tensor maps, argument checks) is at the end
 // of this file and is called from capi.cu.
 #include "prefill.cuh"
+#include "softmax.cuh"
 
 namespace b2a {
 
@@ -10,34 +11,6 @@ namespace b2a {
 // which bf16 and the fp32 row sum hold exactly enough. This keeps the
 // TMEM round trip for the O rescale off the common path.
 constexpr float kRescaleThreshold = 8.0f;
-
-__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
-__device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
-
-template <int D>
-__device__ __forceinline__ void prefill_store_chunk(const PrefillParams& p, int b, int h, int grow, int c,
-                                                    const uint32_t (&o)[32], float inv_l) {
-  const long long base = (long long)b * p.o_sb + (long long)h * p.o_sh + (long long)grow * p.o_st + 32 * c;
-  if (p.out_fp32) {
-    float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.o) + base);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      dst[i] = make_float4(u2f(o[4 * i]) * inv_l, u2f(o[4 * i + 1]) * inv_l, u2f(o[4 * i + 2]) * inv_l,
-                           u2f(o[4 * i + 3]) * inv_l);
-    }
-  } else {
-    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.o) + base);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint4 w;
-      w.x = pack_bf16x2(u2f(o[8 * i + 0]) * inv_l, u2f(o[8 * i + 1]) * inv_l);
-      w.y = pack_bf16x2(u2f(o[8 * i + 2]) * inv_l, u2f(o[8 * i + 3]) * inv_l);
-      w.z = pack_bf16x2(u2f(o[8 * i + 4]) * inv_l, u2f(o[8 * i + 5]) * inv_l);
-      w.w = pack_bf16x2(u2f(o[8 * i + 6]) * inv_l, u2f(o[8 * i + 7]) * inv_l);
-      dst[i] = w;
-    }
-  }
-}
 
 template <int D>
 __global__ void __launch_bounds__(384, 1)
@@ -68,14 +41,22 @@ __global__ void __launch_bounds__(384, 1)
   const int hk = h / (p.Hq / p.Hkv);
   const int q0 = qblk * 256;
   const int sp = p.start_pos_arr ? p.start_pos_arr[b] : p.start_pos;
-  int n_kv;
-  if (p.causal) {
-    const int last_row = min(q0 + 255, p.Tq - 1);
-    const long long kv_end = min((long long)p.Tk, (long long)sp + last_row + 1);
-    n_kv = kv_end <= 0 ? 0 : (int)((kv_end + C::BN - 1) / C::BN);
-  } else {
-    n_kv = (p.Tk + C::BN - 1) / C::BN;
+  // Key blocks each query tile needs: n_t[t] for tile t; tile 0 (earlier rows)
+  // never needs more blocks than tile 1, and under the causal mask at most one
+  // fewer. n_kv = n_t[1] is what gets loaded.
+  int n_t[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    if (p.causal) {
+      const int last_row = min(q0 + (t + 1) * C::BM - 1, p.Tq - 1);
+      const long long kv_end = min((long long)p.Tk, (long long)sp + last_row + 1);
+      n_t[t] = kv_end <= 0 ? 0 : (int)((kv_end + C::BN - 1) / C::BN);
+    } else {
+      n_t[t] = (p.Tk + C::BN - 1) / C::BN;
+    }
   }
+  const int n_kv = n_t[1];
+  const int n0 = n_t[0];
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
@@ -108,6 +89,10 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
+  // Each role's code sits entirely inside the branch that set its register
+  // budget, so the compiler allocates it against that budget.
+  if (warp < 4) {
+  setmaxnreg_dec<C::REGS_LOW>();
   if (n_kv > 0 && warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -144,44 +129,51 @@ __global__ void __launch_bounds__(384, 1)
     if (lane == 0) {
       constexpr uint32_t IDESC_S = umma_idesc_bf16(128, C::BN, false);
       constexpr uint32_t IDESC_PV = umma_idesc_bf16(128, D, true);
-      const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV), sPa = smem_u32(sP);
+      // Descriptors are built once; stepping through a tile adds the byte
+      // offset >> 4 to the 14-bit start-address field (smem addresses stay
+      // below 256 KB, so the field never carries into the next one).
+      const uint64_t dQ = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t dK = make_sdesc_sw128(smem_u32(sKV), 16, 1024);
+      const uint64_t dP = make_sdesc_sw128(smem_u32(sP), 16, 1024);
+      const uint64_t dV = make_sdesc_sw128(smem_u32(sKV), C::CHUNK_BYTES, 1024);
       // S_t = Q_t K^T: A = Q tile (K-major), B = K tile (K-major); 16-wide K
       // steps walk 32 bytes inside a 128-byte swizzle row, then the next chunk.
       auto issue_S = [&](int t, int slot) {
-        const uint32_t qa = sQa + t * C::Q_TILE_BYTES;
-        const uint32_t ka = sKVa + slot * C::KV_TILE_BYTES;
+        const uint64_t qa = dQ + (uint64_t)((t * C::Q_TILE_BYTES) >> 4);
+        const uint64_t ka = dK + (uint64_t)((slot * C::KV_TILE_BYTES) >> 4);
         const uint32_t d = tmem + C::S_COL + t * C::BN;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k >> 2) * C::CHUNK_BYTES + (k & 3) * 32;
-          umma_bf16_ss(d, make_sdesc_sw128(qa + off, 16, 1024), make_sdesc_sw128(ka + off, 16, 1024), IDESC_S,
-                       k > 0 ? 1u : 0u);
+          const uint64_t off = (uint64_t)(((k >> 2) * C::CHUNK_BYTES + (k & 3) * 32) >> 4);
+          umma_bf16_ss(d, qa + off, ka + off, IDESC_S, k > 0 ? 1u : 0u);
         }
       };
       // O_t (+)= P_t V: A = P tile (K-major over keys), B = V tile read
       // MN-major (head_dim contiguous); a 16-key step is 16 rows = 2048 bytes,
-      // 64-column head_dim chunks sit CHUNK_BYTES apart.
+      // 64-column head_dim chunks sit CHUNK_BYTES apart (the LBO of dV).
       auto issue_PV = [&](int t, int slot, bool acc) {
-        const uint32_t pa = sPa + t * C::P_TILE_BYTES;
-        const uint32_t va = sKVa + slot * C::KV_TILE_BYTES;
+        const uint64_t pa = dP + (uint64_t)((t * C::P_TILE_BYTES) >> 4);
+        const uint64_t va = dV + (uint64_t)((slot * C::KV_TILE_BYTES) >> 4);
         const uint32_t d = tmem + C::O_COL + t * D;
 #pragma unroll
         for (int s = 0; s < C::BN / 16; ++s) {
-          const uint32_t aoff = (s >> 2) * C::CHUNK_BYTES + (s & 3) * 32;
-          umma_bf16_ss(d, make_sdesc_sw128(pa + aoff, 16, 1024),
-                       make_sdesc_sw128(va + s * 2048, C::CHUNK_BYTES, 1024), IDESC_PV,
-                       (acc || s > 0) ? 1u : 0u);
+          const uint64_t aoff = (uint64_t)(((s >> 2) * C::CHUNK_BYTES + (s & 3) * 32) >> 4);
+          umma_bf16_ss(d, pa + aoff, va + (uint64_t)((s * 2048) >> 4), IDESC_PV, (acc || s > 0) ? 1u : 0u);
         }
       };
       auto wait_load = [&](int i) -> bool {
         return mbar_wait(&bars->kv_full[i % C::STAGES], (uint32_t)(i / C::STAGES) & 1u, abort_flag, p.err);
       };
 
+      // Tile 0 runs n0 blocks, tile 1 runs n_kv (n0 <= n_kv): a tile-0 block
+      // that lies entirely above the diagonal is neither computed nor waited on.
       bool ok = mbar_wait(&bars->q_full, 0, abort_flag, p.err) && wait_load(0);
       if (ok) {
         tc_fence_after();
-        issue_S(0, 0);
-        tc_commit(&bars->s_full[0]);
+        if (n0 > 0) {
+          issue_S(0, 0);
+          tc_commit(&bars->s_full[0]);
+        }
         issue_S(1, 0);
         tc_commit(&bars->s_full[1]);
         tc_commit(&bars->kv_empty[0]);
@@ -189,18 +181,22 @@ __global__ void __launch_bounds__(384, 1)
           const int vi = 2 * j + 1;
           const int vslot = vi % C::STAGES;
           if (!wait_load(vi)) break;
-          if (!mbar_wait(&bars->p_full[0], (uint32_t)j & 1u, abort_flag, p.err)) break;
-          tc_fence_after();
-          issue_PV(0, vslot, j > 0);
-          if (j + 1 == n_kv) tc_commit(&bars->o_full[0]);
+          if (j < n0) {
+            if (!mbar_wait(&bars->p_full[0], (uint32_t)j & 1u, abort_flag, p.err)) break;
+            tc_fence_after();
+            issue_PV(0, vslot, j > 0);
+            if (j + 1 == n0) tc_commit(&bars->o_full[0]);
+          }
           int kslot = 0;
           if (j + 1 < n_kv) {
             const int ki = 2 * j + 2;
             kslot = ki % C::STAGES;
             if (!wait_load(ki)) break;
             tc_fence_after();
-            issue_S(0, kslot);
-            tc_commit(&bars->s_full[0]);
+            if (j + 1 < n0) {
+              issue_S(0, kslot);
+              tc_commit(&bars->s_full[0]);
+            }
           }
           if (!mbar_wait(&bars->p_full[1], (uint32_t)j & 1u, abort_flag, p.err)) break;
           tc_fence_after();
@@ -219,7 +215,9 @@ __global__ void __launch_bounds__(384, 1)
       tc_commit(&bars->drain);
       mbar_wait_quiet(&bars->drain, 0);
     }
-  } else if (warp >= 4) {
+  }
+  } else {
+    setmaxnreg_inc<C::REGS_HIGH>();
     // ------------------------------------------------------------ softmax + epilogue
     const int t = (warp - 4) >> 2;
     const int wq = warp & 3;
@@ -236,8 +234,9 @@ __global__ void __launch_bounds__(384, 1)
     float l_run = 0.f;
     const uint32_t pbase = smem_u32(sP) + t * C::P_TILE_BYTES;
     bool ok = true;
+    const int n_mine = t == 0 ? n0 : n_kv;
 
-    for (int j = 0; j < n_kv; ++j) {
+    for (int j = 0; j < n_mine; ++j) {
       const bool w = mbar_wait(&bars->s_full[t], (uint32_t)j & 1u, abort_flag, p.err);
       if (!__all_sync(0xffffffffu, w)) {
         ok = false;
@@ -248,26 +247,26 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
       for (int q = 0; q < 4; ++q) tmem_ld32(tS + 32 * q, s[q]);
       tmem_wait_ld();
+#define S_AT(i) u2f(s[(i) >> 5][(i) & 31])
 
+      // Mask only on blocks that cross this row's last visible key.
       const long long lim_ll = kv_last - (long long)j * C::BN;
       const int lim = lim_ll < -1 ? -1 : (lim_ll > C::BN - 1 ? C::BN - 1 : (int)lim_ll);
-      float mx = -INFINITY;
-      if (lim == C::BN - 1) {
+      if (lim < C::BN - 1) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, u2f(s[q][i]));
-      } else {
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float v = u2f(s[q][i]);
-            if (32 * q + i > lim) v = -INFINITY;
-            s[q][i] = f2u(v);
-            mx = fmaxf(mx, v);
-          }
+        for (int i = 0; i < C::BN; ++i)
+          if (i > lim) s[i >> 5][i & 31] = f2u(-INFINITY);
       }
+      // Row max: four independent chains of 3-input max.
+      float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < C::BN; i += 8) {
+        a0 = fmax3(a0, S_AT(i), S_AT(i + 1));
+        a1 = fmax3(a1, S_AT(i + 2), S_AT(i + 3));
+        a2 = fmax3(a2, S_AT(i + 4), S_AT(i + 5));
+        a3 = fmax3(a3, S_AT(i + 6), S_AT(i + 7));
+      }
+      const float mx = fmaxf(fmax3(a0, a1, a2), a3);
       const float m_blk = mx * sl2;
       const float m_new = fmaxf(m_run, m_blk);
       bool rescale = false;
@@ -283,21 +282,11 @@ __global__ void __launch_bounds__(384, 1)
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
 
       // P = exp2(S * scale * log2e - m), bf16, into the swizzled K-major tile.
-      float rs = 0.f;
-#pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
-        float pv[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          pv[i] = ex2(fmaf(u2f(s[c8 >> 2][(c8 & 3) * 8 + i]), sl2, -m_use));
-          rs += pv[i];
-        }
-        const int region = c8 >> 3, jj = c8 & 7;
-        const uint32_t addr = pbase + region * C::CHUNK_BYTES + row * 128 + ((jj ^ (row & 7)) << 4);
-        st_shared_v4(addr, pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]), pack_bf16x2(pv[4], pv[5]),
-                     pack_bf16x2(pv[6], pv[7]));
-      }
-      l_run += rs;
+      if (lim == C::BN - 1)
+        l_run += softmax_p_row<C::BN, true>(s, sl2, m_use, pbase, C::CHUNK_BYTES, row);
+      else
+        l_run += softmax_p_row<C::BN, false>(s, sl2, m_use, pbase, C::CHUNK_BYTES, row);
+#undef S_AT
 
       // O_t holds the sum through block j-1 (its last PV finished before
       // S_t(j) did); rescale it before the MMA adds block j.
@@ -318,13 +307,13 @@ __global__ void __launch_bounds__(384, 1)
       mbar_arrive(&bars->p_full[t]);
     }
 
-    if (n_kv == 0) {
+    if (n_mine == 0) {
       if (valid) {
         uint32_t z[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) z[i] = 0u;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) prefill_store_chunk<D>(p, b, h, grow, c, z, 0.f);
+        for (int c = 0; c < D / 32; ++c) store_out_chunk(p, b, h, grow, c, z, 0.f);
         if (p.lse) p.lse[((long long)b * p.Hq + h) * p.Tq + grow] = -INFINITY;
       }
     } else if (ok) {
@@ -337,7 +326,7 @@ __global__ void __launch_bounds__(384, 1)
           uint32_t o[32];
           tmem_ld32(tO + 32 * c, o);
           tmem_wait_ld();
-          if (valid) prefill_store_chunk<D>(p, b, h, grow, c, o, inv_l);
+          if (valid) store_out_chunk(p, b, h, grow, c, o, inv_l);
         }
         if (p.lse && valid) {
           p.lse[((long long)b * p.Hq + h) * p.Tq + grow] =
@@ -364,6 +353,10 @@ static int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const 
   cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM_BYTES);
   if (e != cudaSuccess) return -1;
+  // The in-kernel register split needs at least MIN_LAUNCH_REGS per thread.
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, fa_prefill_kernel<D>) != cudaSuccess || fa.numRegs < C::MIN_LAUNCH_REGS)
+    return -1;
   const long long nblk = (long long)p.n_qblk * p.Hq * p.B;
   if (nblk <= 0 || nblk > 0x7fffffffLL) return -2;
   fa_prefill_kernel<D><<<(unsigned)nblk, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, p);

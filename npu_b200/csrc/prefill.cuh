@@ -61,6 +61,13 @@ struct PrefillCfg {
   static constexpr int S_COL = 0;          // S_t at S_COL + t * BN
   static constexpr int O_COL = NQT * BN;   // O_t at O_COL + t * D
   static constexpr int THREADS = 384;
+  // setmaxnreg split: warpgroup 0 (TMA + MMA issue) gives registers to the
+  // two softmax warpgroups. 128 * REGS_LOW + 256 * REGS_HIGH = 61440 = 384 * 160,
+  // so any launch with >= MIN_LAUNCH_REGS registers per thread covers it (the
+  // launcher refuses to launch otherwise).
+  static constexpr int REGS_LOW = 112;
+  static constexpr int REGS_HIGH = 184;
+  static constexpr int MIN_LAUNCH_REGS = (128 * REGS_LOW + 256 * REGS_HIGH + THREADS - 1) / THREADS;
   static_assert(D == 64 || D == 128, "two-tile prefill supports head_dim 64 and 128");
   static_assert(O_COL + NQT * D <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -78,6 +85,10 @@ struct PrefillBars {
   uint32_t tmem_base;
   int abort_flag;
 };
+
+// Head dim 256 variant (one query tile per CTA, prefill_d256.cu).
+int launch_prefill_d256(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                        const PrefillParams& p, cudaStream_t st);
 
 // Launch the prefill kernel on `st`. Returns 0 on success, -3 for an
 // unsupported head_dim, another negative value on launch failure.

@@ -1,0 +1,129 @@
+// Device helpers shared by the prefill kernels (prefill.cu, prefill_d256.cu):
+// the exp2 split between the MUFU and FMA pipes, 3-input max, and the output
+// store of one 32-column chunk of a query row.
+#pragma once
+
+#include "prefill.cuh"
+
+namespace b2a {
+
+// Of every 4 column pairs of S, this many have their exp2 evaluated on the
+// FMA pipe (exp2_fma2) instead of the MUFU unit; the rest use ex2.approx.
+// Spreading the exponentials over both pipes keeps MUFU off the critical path.
+#ifndef B2A_EXP2_EMU
+#define B2A_EXP2_EMU 1
+#endif
+constexpr int kExp2EmuPairs = B2A_EXP2_EMU;
+static_assert(kExp2EmuPairs >= 0 && kExp2EmuPairs <= 4, "B2A_EXP2_EMU is a count out of 4 pairs");
+
+__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
+__device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+#ifndef B2A_EXP2_DEG
+#define B2A_EXP2_DEG 3
+#endif
+static_assert(B2A_EXP2_DEG == 2 || B2A_EXP2_DEG == 3, "exp2 polynomial degree is 2 or 3");
+
+// 2^x for a pair, on the FMA pipe: x = n + f with n = round(x) (adding the
+// 1.5 * 2^23 rounding constant leaves n in the low mantissa bits of t) and
+// f in [-1/2, 1/2]; 2^f comes from a polynomial fitted for relative error by
+// npu_b200/csrc/exp2_poly_fit.py (cubic: max rel. error 7.5e-5; quadratic:
+// 1.7e-3, below the 2^-9 rounding of the bf16 P tile); 2^n is added to the
+// exponent field with one shift-add of n << 23. Inputs are clamped at -120 so
+// the exponent arithmetic cannot wrap. The caller only uses this on key
+// blocks without masked entries (no -inf inputs); it returns 2^-120, not 0,
+// for anything below the clamp.
+__device__ __forceinline__ uint32_t shl23_add(uint32_t t, uint32_t p) {
+  uint32_t r;
+  asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(r) : "r"(t), "r"(p));
+  return r;
+}
+
+__device__ __forceinline__ float2 exp2_fma2(float2 xin) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  const float2 x = make_float2(fmaxf(xin.x, -120.f), fmaxf(xin.y, -120.f));
+  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+  const float2 n = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+#if B2A_EXP2_DEG == 3
+  constexpr float c0 = 9.999281168e-01f, c1 = 6.932609677e-01f, c2 = 2.426105440e-01f, c3 = 5.517132208e-02f;
+  float2 p = __ffma2_rn(f, make_float2(c3, c3), make_float2(c2, c2));
+  p = __ffma2_rn(p, f, make_float2(c1, c1));
+  p = __ffma2_rn(p, f, make_float2(c0, c0));
+#else
+  constexpr float c0 = 1.000442982e+00f, c1 = 7.034428120e-01f, c2 = 2.384257019e-01f;
+  float2 p = __ffma2_rn(f, make_float2(c2, c2), make_float2(c1, c1));
+  p = __ffma2_rn(p, f, make_float2(c0, c0));
+#endif
+  return make_float2(__uint_as_float(shl23_add(__float_as_uint(t.x), __float_as_uint(p.x))),
+                     __uint_as_float(shl23_add(__float_as_uint(t.y), __float_as_uint(p.y))));
+}
+
+// One row of P for a key block: x = S * scale * log2e - m, P = 2^x as bf16
+// into the 128B-swizzled K-major tile (16-byte stores, chunk index XOR row),
+// returns the fp32 row sum. With kEmu, kExp2EmuPairs of every 4 column pairs
+// take exp2 on the FMA pipe; callers pass kEmu only for blocks with no masked
+// key (all x finite), the others use ex2.approx throughout (exact 0 for -inf).
+template <int BN, bool kEmu>
+__device__ __forceinline__ float softmax_p_row(const uint32_t (&s)[BN / 32][32], float sl2, float m_use,
+                                               uint32_t pbase, int chunk_bytes, int row) {
+  const float2 sc2 = make_float2(sl2, sl2);
+  const float2 nm2 = make_float2(-m_use, -m_use);
+  float2 acc[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) acc[k] = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int c8 = 0; c8 < BN / 8; ++c8) {
+    uint32_t wv[4];
+#pragma unroll
+    for (int pp = 0; pp < 4; ++pp) {
+      const int i = c8 * 8 + pp * 2;
+      const float2 x = __ffma2_rn(make_float2(u2f(s[i >> 5][i & 31]), u2f(s[(i + 1) >> 5][(i + 1) & 31])), sc2, nm2);
+      float2 e;
+      if (kEmu && pp < kExp2EmuPairs)
+        e = exp2_fma2(x);
+      else
+        e = make_float2(ex2(x.x), ex2(x.y));
+      acc[pp] = __fadd2_rn(acc[pp], e);
+      wv[pp] = pack_bf16x2(e.x, e.y);
+    }
+    st_shared_v4(pbase + (c8 >> 3) * chunk_bytes + row * 128 + (((c8 & 7) ^ (row & 7)) << 4), wv[0], wv[1], wv[2],
+                 wv[3]);
+  }
+  const float2 r2 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+  return r2.x + r2.y;
+}
+
+// Scale one 32-column chunk of an output row by inv_l and store it (fp32 or
+// bf16) with 16-byte stores.
+__device__ __forceinline__ void store_out_chunk(const PrefillParams& p, int b, int h, int grow, int c,
+                                                const uint32_t (&o)[32], float inv_l) {
+  const long long base = (long long)b * p.o_sb + (long long)h * p.o_sh + (long long)grow * p.o_st + 32 * c;
+  if (p.out_fp32) {
+    float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.o) + base);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      dst[i] = make_float4(u2f(o[4 * i]) * inv_l, u2f(o[4 * i + 1]) * inv_l, u2f(o[4 * i + 2]) * inv_l,
+                           u2f(o[4 * i + 3]) * inv_l);
+    }
+  } else {
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.o) + base);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 w;
+      w.x = pack_bf16x2(u2f(o[8 * i + 0]) * inv_l, u2f(o[8 * i + 1]) * inv_l);
+      w.y = pack_bf16x2(u2f(o[8 * i + 2]) * inv_l, u2f(o[8 * i + 3]) * inv_l);
+      w.z = pack_bf16x2(u2f(o[8 * i + 4]) * inv_l, u2f(o[8 * i + 5]) * inv_l);
+      w.w = pack_bf16x2(u2f(o[8 * i + 6]) * inv_l, u2f(o[8 * i + 7]) * inv_l);
+      dst[i] = w;
+    }
+  }
+}
+
+}  // namespace b2a

@@ -32,8 +32,8 @@ class NpuAttention:
 
     def __init__(self, BR: int = 128, BC: int = 32, D: int = 64, n_cores: Optional[int] = None,
                  device: Optional[torch.device] = None, out_dtype: torch.dtype = torch.bfloat16):
-        if D not in (64, 128):
-            raise ValueError(f"head_dim {D} not supported by the prefill kernel (64, 128)")
+        if D not in (64, 128, 256):
+            raise ValueError(f"head_dim {D} not supported by the prefill kernels (64, 128, 256)")
         self.BR, self.BC, self.D = BR, BC, D
         self.n_cores = n_cores
         self.device = torch.device(device) if device is not None else None

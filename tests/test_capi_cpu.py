@@ -64,7 +64,7 @@ def test_prefill_argument_validation():
     assert _prefill(scale=0.0) == _lib.B2A_ERR_INVALID_ARG
     assert _prefill(scale=float("nan")) == _lib.B2A_ERR_INVALID_ARG
     assert _prefill(D=96) == _lib.B2A_ERR_HEAD_DIM
-    assert _prefill(D=256) == _lib.B2A_ERR_HEAD_DIM
+    assert _prefill(D=512) == _lib.B2A_ERR_HEAD_DIM
     assert _prefill(Hkv=3) == _lib.B2A_ERR_GQA
     assert _prefill(q=FAKE + 2) == _lib.B2A_ERR_ALIGNMENT
     assert _prefill(qs=(8 * 64 * 128, 64 * 128, 100)) == _lib.B2A_ERR_ALIGNMENT

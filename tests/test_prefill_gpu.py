@@ -83,6 +83,13 @@ CASES = [
     (2, 4, 4, 200, 333, 128, 0, False),
     (1, 2, 1, 1000, 1000, 128, 0, True),
     (1, 32, 4, 512, 512, 128, 0, True),
+    # head_dim 256 (Qwen3.6 geometry, one-tile kernel with 64-key blocks)
+    (1, 2, 1, 1, 1, 256, 0, True),
+    (1, 4, 2, 65, 65, 256, 0, True),
+    (2, 16, 2, 129, 129, 256, 0, True),
+    (1, 8, 1, 200, 700, 256, 500, True),
+    (1, 2, 2, 300, 333, 256, 0, False),
+    (1, 16, 2, 1000, 1000, 256, 0, True),
 ]
 
 
@@ -197,3 +204,20 @@ def test_no_device_error_left(cuda_dev):
     from npu_b200 import api
 
     assert api.device_error(clear=True) == 0
+
+
+def test_config5_geometry_sampled_rows(cuda_dev):
+    """Config 5 head geometry (16 query / 2 KV heads, D=256, scale 1/16) on a
+    16k-token causal prefill: sampled rows against the oracle."""
+    from npu_b200 import api
+
+    T = 16384
+    g = torch.Generator().manual_seed(5)
+    q, k, v = _rand((1, 16, T, 256), g, cuda_dev), _rand((1, 2, T, 256), g, cuda_dev), _rand((1, 2, T, 256), g, cuda_dev)
+    out = api.prefill(q, k, v, scale=1 / 16)
+    qc, kc, vc = q.cpu(), k.cpu(), v.cpu()
+    rows = [0, 63, 64, 127, 128, 4097, T // 2, T - 65, T - 1]
+    for h in (0, 7, 8, 15):
+        ref = A.prefill_rows_ref(qc, kc, vc, 0, h, rows, scale=1 / 16)
+        assert (out[0, h, rows].cpu() - ref).abs().max().item() <= TOL
+    assert torch.isfinite(out).all()
