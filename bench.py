@@ -8,7 +8,9 @@ scale 1/sqrt(128)); the (batch x KV-head) units are split across the N GPUs
 with no collective (strong scaling: total work fixed). A step is one launch
 over the whole batch. `decode` reports config 4 (128 sequences, one query
 token, lengths ~ U[1024, 32768], HBM GB/s) the same way; `sweep` reports the
-config 3 prefill at T=512 and T=2048.
+config 3 prefill at T=512 and T=2048; `long_context` reports config 5 (one
+131072-token sequence, D=256; zig-zag context parallel with a NCCL K/V
+all-gather when N > 1).
 
 Timing: W untimed steps, then K steps bracketed by barrier + synchronize,
 CUDA events on the launching stream, max over ranks. Inputs are larger than
@@ -259,6 +261,7 @@ def run_ours(a, dist: Dist) -> dict | None:
     torch.cuda.empty_cache()
 
     decode = run_decode(a, dist, dev, pk) if a.decode else None
+    long_ctx = run_long_context(a, dist, dev, pk) if a.long else None
 
     cpu = None
     if rank == 0 and world == 1 and a.cpu_baseline:
@@ -288,6 +291,7 @@ def run_ours(a, dist: Dist) -> dict | None:
         "device_error": err,
         "sweep": sweep,
         "decode": decode,
+        "long_context": long_ctx,
         "cpu_baseline": cpu,
     }
     return line
@@ -328,6 +332,49 @@ def run_decode(a, dist: Dist, dev, pk) -> dict:
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "kernel": "decode_split_kernel<128> + decode_combine_kernel",
                          "traffic": load_traffic("decode_cfg4", B=Bm), "launch_ms": per_ms}}
+
+
+def run_long_context(a, dist: Dist, dev, pk) -> dict:
+    """Config 5: one sequence of T=131072, 16 query / 2 KV heads, D=256, causal.
+    One GPU runs it whole; N GPUs split the query rows zig-zag (rank g owns
+    chunks g and 2N-1-g) and all-gather K/V with NCCL once per step."""
+    from npu_b200 import api
+    from npu_b200.dist import ContextParallelPrefill, causal_flops_rows
+
+    T, Hq, Hkv, D = a.long_T, 16, 2, 256
+    scale = 1.0 / 16
+    world, rank = dist.world, dist.rank
+    g = torch.Generator(device=dev).manual_seed(3000 + rank)
+    rows = T if world == 1 else T // world
+    q = torch.randn(1, Hq, rows, D, device=dev, generator=g, dtype=torch.bfloat16)
+    k = torch.randn(1, Hkv, rows, D, device=dev, generator=g, dtype=torch.bfloat16)
+    v = torch.randn(1, Hkv, rows, D, device=dev, generator=g, dtype=torch.bfloat16)
+    if world == 1:
+        o = torch.empty_like(q)
+
+        def step():
+            api.prefill(q, k, v, scale=scale, out=o, out_dtype=torch.bfloat16)
+
+        mine = causal_flops_rows((0, T), D, Hq)
+        launches = 1
+    else:
+        cp = ContextParallelPrefill(T, world, rank, group=None)
+
+        def step():
+            cp.run(q, k, v, scale=scale, out_dtype=torch.bfloat16)
+
+        mine = sum(causal_flops_rows(c, D, Hq) for c in cp.chunks)
+        launches = 2
+    total_ms, per_ms = timed(step, a.steps, a.warmup, dist)
+    flops = causal_flops_rows((0, T), D, Hq)
+    peak = float(pk["bf16_tflops"])
+    del q, k, v
+    torch.cuda.empty_cache()
+    return {"metric": "long-context causal prefill attention TFLOP/s (config 5)", "value":
+            flops * a.steps / (total_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": total_ms / a.steps,
+            "T": T, "Hq": Hq, "Hkv": Hkv, "D": D, "gpu_launches": launches * a.steps,
+            "parallelism": "single GPU" if world == 1 else f"zig-zag context parallel x{world}, NCCL all-gather of K/V",
+            "rank0_frac_of_peak": (mine / (per_ms * 1e-3) / 1e12) / peak, "scaling": "strong"}
 
 
 def load_traffic(key: str, **kw):
@@ -410,6 +457,8 @@ def main():
     ap.add_argument("--T", type=int, default=8192)
     ap.add_argument("--sweep", type=lambda s: [int(x) for x in s.split(",") if x], default=[512, 2048])
     ap.add_argument("--no-decode", dest="decode", action="store_false")
+    ap.add_argument("--no-long", dest="long", action="store_false")
+    ap.add_argument("--long-T", type=int, default=131072)
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")

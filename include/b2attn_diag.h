@@ -17,6 +17,7 @@ extern "C" {
  * a: [128][128] bf16 row-major (M x K).
  * b_mn_major = 0: b is [N][K] row-major and c = a * b^T.
  * b_mn_major = 1: b is [K][N] row-major and c = a * b.
+ * b_mn_major = 2: as 1, with a read by the MMA from tensor memory.
  * Returns 0 or a negative B2A_ERR_* code.
  */
 B2A_API int b2a_diag_umma_gemm(const void* a, const void* b, float* c, int b_mn_major, void* stream);

@@ -3,8 +3,10 @@
 // wrong GEMM rather than as a wrong attention output.
 //   b_mn_major = 0: C = A * B^T with B given as [N=128][K=128] (the S = Q K^T path)
 //   b_mn_major = 1: C = A * B   with B given as [K=128][N=128] (the O = P V path)
+//   b_mn_major = 2: as 1, but A is read from TMEM (the P-in-TMEM path): each
+//                   thread stores its row of A into TMEM with tcgen05.st.
 // A is [M=128][K=128] row-major. Operands are written into shared memory by
-// threads using the 128-byte swizzle formula (as the P tile is).
+// threads using the 128-byte swizzle formula.
 #include "b2attn_diag.h"
 #include "common.cuh"
 
@@ -40,18 +42,37 @@ __global__ void __launch_bounds__(128) diag_umma_kernel(const __nv_bfloat16* A, 
     fence_mbar_init();
   }
   fence_proxy_async_smem();
-  if (warp == 0) tmem_alloc(tmem_slot, 128);
+  if (warp == 0) tmem_alloc(tmem_slot, 256);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  constexpr uint32_t kACol = 128;  // A (packed bf16) at TMEM columns [128, 192)
+  if (b_mn == 2) {
+    const uint32_t* arow = reinterpret_cast<const uint32_t*>(A) + tid * 64;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t r[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) r[i] = arow[half * 32 + i];
+      tmem_st32(tmem + lane_off + kACol + half * 32, r);
+    }
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   if (tid == 0) {
     const uint32_t a = smem_u32(sA), b = smem_u32(sB);
     const uint32_t idesc = umma_idesc_bf16(128, 128, b_mn != 0);
     for (int k = 0; k < 8; ++k) {
       const uint32_t off = (k >> 2) * CH + (k & 3) * 32;
       const uint64_t bd = b_mn ? make_sdesc_sw128(b + k * 2048, CH, 1024) : make_sdesc_sw128(b + off, 16, 1024);
-      umma_bf16_ss(tmem, make_sdesc_sw128(a + off, 16, 1024), bd, idesc, k > 0 ? 1u : 0u);
+      if (b_mn == 2)
+        umma_bf16_ts(tmem, tmem + kACol + k * 8, bd, idesc, k > 0 ? 1u : 0u);
+      else
+        umma_bf16_ss(tmem, make_sdesc_sw128(a + off, 16, 1024), bd, idesc, k > 0 ? 1u : 0u);
     }
     tc_commit(bar);
   }
@@ -74,7 +95,7 @@ __global__ void __launch_bounds__(128) diag_umma_kernel(const __nv_bfloat16* A, 
   if (warp == 0) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 256);
   }
 }
 

@@ -22,7 +22,6 @@ __global__ void __launch_bounds__(384, 1)
   uint8_t* smem = smem_raw + pad;
   uint8_t* sQ = smem + C::OFF_Q;
   uint8_t* sKV = smem + C::OFF_KV;
-  uint8_t* sP = smem + C::OFF_P;
   PrefillBars* bars = reinterpret_cast<PrefillBars*>(smem + C::OFF_BAR);
   volatile int* abort_flag = &bars->abort_flag;
 
@@ -134,7 +133,6 @@ __global__ void __launch_bounds__(384, 1)
       // below 256 KB, so the field never carries into the next one).
       const uint64_t dQ = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
       const uint64_t dK = make_sdesc_sw128(smem_u32(sKV), 16, 1024);
-      const uint64_t dP = make_sdesc_sw128(smem_u32(sP), 16, 1024);
       const uint64_t dV = make_sdesc_sw128(smem_u32(sKV), C::CHUNK_BYTES, 1024);
       // S_t = Q_t K^T: A = Q tile (K-major), B = K tile (K-major); 16-wide K
       // steps walk 32 bytes inside a 128-byte swizzle row, then the next chunk.
@@ -148,18 +146,16 @@ __global__ void __launch_bounds__(384, 1)
           umma_bf16_ss(d, qa + off, ka + off, IDESC_S, k > 0 ? 1u : 0u);
         }
       };
-      // O_t (+)= P_t V: A = P tile (K-major over keys), B = V tile read
-      // MN-major (head_dim contiguous); a 16-key step is 16 rows = 2048 bytes,
-      // 64-column head_dim chunks sit CHUNK_BYTES apart (the LBO of dV).
+      // O_t (+)= P_t V: A = P_t in TMEM (16 keys = 8 columns per step), B = V
+      // tile read MN-major (head_dim contiguous); a 16-key step is 16 rows =
+      // 2048 bytes, 64-column head_dim chunks sit CHUNK_BYTES apart (LBO of dV).
       auto issue_PV = [&](int t, int slot, bool acc) {
-        const uint64_t pa = dP + (uint64_t)((t * C::P_TILE_BYTES) >> 4);
+        const uint32_t pa = tmem + C::S_COL + t * C::BN;
         const uint64_t va = dV + (uint64_t)((slot * C::KV_TILE_BYTES) >> 4);
         const uint32_t d = tmem + C::O_COL + t * D;
 #pragma unroll
-        for (int s = 0; s < C::BN / 16; ++s) {
-          const uint64_t aoff = (uint64_t)(((s >> 2) * C::CHUNK_BYTES + (s & 3) * 32) >> 4);
-          umma_bf16_ss(d, pa + aoff, va + (uint64_t)((s * 2048) >> 4), IDESC_PV, (acc || s > 0) ? 1u : 0u);
-        }
+        for (int s = 0; s < C::BN / 16; ++s)
+          umma_bf16_ts(d, pa + 8 * s, va + (uint64_t)((s * 2048) >> 4), IDESC_PV, (acc || s > 0) ? 1u : 0u);
       };
       auto wait_load = [&](int i) -> bool {
         return mbar_wait(&bars->kv_full[i % C::STAGES], (uint32_t)(i / C::STAGES) & 1u, abort_flag, p.err);
@@ -232,7 +228,6 @@ __global__ void __launch_bounds__(384, 1)
     const float sl2 = p.scale_log2;
     float m_run = -INFINITY;
     float l_run = 0.f;
-    const uint32_t pbase = smem_u32(sP) + t * C::P_TILE_BYTES;
     bool ok = true;
     const int n_mine = t == 0 ? n0 : n_kv;
 
@@ -281,11 +276,12 @@ __global__ void __launch_bounds__(384, 1)
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
 
-      // P = exp2(S * scale * log2e - m), bf16, into the swizzled K-major tile.
-      if (lim == C::BN - 1)
-        l_run += softmax_p_row<C::BN, true>(s, sl2, m_use, pbase, C::CHUNK_BYTES, row);
+      // P = exp2(S * scale * log2e - m), bf16, over the first half of S_t in TMEM.
+      // The pipe choice must be warp-uniform: the stores inside are warp-wide.
+      if (__all_sync(0xffffffffu, lim == C::BN - 1))
+        l_run += softmax_p_row_tmem<C::BN, true>(s, sl2, m_use, tS);
       else
-        l_run += softmax_p_row<C::BN, false>(s, sl2, m_use, pbase, C::CHUNK_BYTES, row);
+        l_run += softmax_p_row_tmem<C::BN, false>(s, sl2, m_use, tS);
 #undef S_AT
 
       // O_t holds the sum through block j-1 (its last PV finished before
@@ -300,9 +296,8 @@ __global__ void __launch_bounds__(384, 1)
           for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * alpha);
           tmem_st32(tO + 32 * c, o);
         }
-        tmem_wait_st();
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();  // P and any O rescale are in TMEM before the MMA may read them
       tc_fence_before();
       mbar_arrive(&bars->p_full[t]);
     }

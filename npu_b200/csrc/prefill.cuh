@@ -18,8 +18,10 @@
 //   warps 4-7   softmax + epilogue for tile 0 (thread = row = TMEM lane)
 //   warps 8-11  softmax + epilogue for tile 1
 // TMEM (512 columns): S_0, S_1 (128 fp32 columns each), O_0, O_1 (D columns).
-// P (bf16) goes through shared memory in the 128B-swizzled K-major layout
-// that the PV UMMA reads as its A operand.
+// P (bf16) is written by the softmax threads into tensor memory over the first
+// half of its own S columns; the PV UMMA reads its A operand from there, so P
+// never touches shared memory (whose bandwidth, shared by the tensor core's
+// operand reads and the TMA fills, is what bounds this kernel).
 #pragma once
 
 #include "common.cuh"
@@ -49,16 +51,14 @@ struct PrefillCfg {
   static constexpr int CHUNK_BYTES = 128 * 128;  // 128 rows x 128 B
   static constexpr int Q_TILE_BYTES = BM * D * 2;
   static constexpr int KV_TILE_BYTES = BN * D * 2;
-  static constexpr int P_TILE_BYTES = BM * BN * 2;
-  static constexpr int STAGES = (D == 64) ? 6 : 3;
+  static constexpr int STAGES = (D == 64) ? 8 : 5;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = OFF_Q + NQT * Q_TILE_BYTES;
-  static constexpr int OFF_P = OFF_KV + STAGES * KV_TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_P + NQT * P_TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_KV + STAGES * KV_TILE_BYTES;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
   static constexpr int TMEM_COLS = 512;
-  static constexpr int S_COL = 0;          // S_t at S_COL + t * BN
+  static constexpr int S_COL = 0;          // S_t at S_COL + t * BN; P_t over its first BN / 2
   static constexpr int O_COL = NQT * BN;   // O_t at O_COL + t * D
   static constexpr int THREADS = 384;
   // setmaxnreg split: warpgroup 0 (TMA + MMA issue) gives registers to the

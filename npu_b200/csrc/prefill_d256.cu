@@ -4,9 +4,13 @@
 // Same semantics as fa_prefill_kernel (prefill.cu). TMEM cannot hold two
 // 128 x 256 fp32 output tiles plus scores, so one CTA owns ONE 128-row query
 // tile and overlaps across key blocks instead of across query tiles:
-//   TMEM: S[0], S[1] (64 fp32 columns each, double-buffered), O (256 columns)
-//   smem: Q (64 KB), a 3-stage ring of 64-key K / V tiles (32 KB each),
-//         P[0], P[1] (128 x 64 bf16, double-buffered)
+//   TMEM: S[0], S[1] (64 fp32 columns each, double-buffered; P[b] is written
+//         over the first 32 columns of S[b]), Q (128 columns of packed bf16,
+//         copied in once), O (256 columns)
+//   smem: Q staging (64 KB), a 5-stage ring of 64-key K / V tiles (32 KB each)
+// Both MMAs take their A operand from TMEM (Q for S = Q K^T, P for O += P V),
+// so shared memory only carries K and V: its bandwidth, shared by the
+// tensor core's operand reads and the TMA fills, is what bounds this kernel.
 // MMA order: S(0), S(1), then per block j: PV(j), S(j+2). While the softmax
 // warpgroup turns S(j) into P(j), the tensor core runs PV(j-1) and S(j+1).
 // Warps: 0 TMA, 1 TMEM + MMA issue, 2-3 idle, 4-7 softmax + epilogue.
@@ -24,15 +28,14 @@ struct D256Cfg {
   static constexpr int KV_CHUNK = BN * 128;           // 8 KB: 64 rows x 128 B
   static constexpr int Q_BYTES = KCH * Q_CHUNK;       // 64 KB
   static constexpr int KV_TILE_BYTES = KCH * KV_CHUNK;  // 32 KB
-  static constexpr int P_TILE_BYTES = BM * BN * 2;    // 16 KB (one chunk)
-  static constexpr int STAGES = 3;
+  static constexpr int STAGES = 5;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = OFF_Q + Q_BYTES;
-  static constexpr int OFF_P = OFF_KV + STAGES * KV_TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_P + 2 * P_TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_KV + STAGES * KV_TILE_BYTES;
   static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
   static constexpr int TMEM_COLS = 512;
-  static constexpr int S_COL = 0;    // S[b] at b * BN
+  static constexpr int S_COL = 0;    // S[b] at b * BN, P[b] over its first BN / 2
+  static constexpr int Q_COL = 128;  // Q (bf16 pairs) at 128 .. 255
   static constexpr int O_COL = 256;  // O at 256 .. 511
   static constexpr int THREADS = 256;  // 1 CTA per SM: up to 255 registers per thread
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -40,8 +43,9 @@ struct D256Cfg {
 
 struct D256Bars {
   uint64_t q_full;
-  uint64_t kv_full[4];
-  uint64_t kv_empty[4];
+  uint64_t q_tmem;
+  uint64_t kv_full[8];
+  uint64_t kv_empty[8];
   uint64_t s_full[2];
   uint64_t p_full[2];
   uint64_t pv_done;
@@ -86,7 +90,6 @@ __global__ void __launch_bounds__(256, 1)
   uint8_t* smem = smem_raw + pad;
   uint8_t* sQ = smem + C::OFF_Q;
   uint8_t* sKV = smem + C::OFF_KV;
-  uint8_t* sP = smem + C::OFF_P;
   D256Bars* bars = reinterpret_cast<D256Bars*>(smem + C::OFF_BAR);
   volatile int* abort_flag = &bars->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -112,6 +115,7 @@ __global__ void __launch_bounds__(256, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->q_tmem, 128);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&bars->kv_full[s], 1);
       mbar_init(&bars->kv_empty[s], 1);
@@ -168,9 +172,7 @@ __global__ void __launch_bounds__(256, 1)
       // -------------------------------------------------------- UMMA issuer
       constexpr uint32_t IDESC_S = umma_idesc_bf16(128, C::BN, false);
       constexpr uint32_t IDESC_PV = umma_idesc_bf16(128, C::D, true);
-      const uint64_t dQ = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
       const uint64_t dK = make_sdesc_sw128(smem_u32(sKV), 16, 1024);
-      const uint64_t dP = make_sdesc_sw128(smem_u32(sP), 16, 1024);
       const uint64_t dV = make_sdesc_sw128(smem_u32(sKV), C::KV_CHUNK, 1024);
       int li = 0;  // next load item to consume
       auto wait_item = [&]() -> int {
@@ -179,28 +181,28 @@ __global__ void __launch_bounds__(256, 1)
         ++li;
         return ok ? slot : -1;
       };
-      // S[buf] = Q K^T: 16 K-steps of 16 over D=256 (4 chunks of 128 B rows).
+      // S[buf] = Q K^T: A = Q in TMEM (8 columns per 16-wide K-step), B = the
+      // K tile in smem (4 chunks of 128 B rows, 32 B per K-step inside one).
       auto issue_S = [&](int buf, int slot) {
         const uint64_t ka = dK + (uint64_t)((slot * C::KV_TILE_BYTES) >> 4);
         const uint32_t d = tmem + C::S_COL + buf * C::BN;
 #pragma unroll
         for (int k = 0; k < C::D / 16; ++k) {
-          const uint64_t qo = (uint64_t)(((k >> 2) * C::Q_CHUNK + (k & 3) * 32) >> 4);
           const uint64_t ko = (uint64_t)(((k >> 2) * C::KV_CHUNK + (k & 3) * 32) >> 4);
-          umma_bf16_ss(d, dQ + qo, ka + ko, IDESC_S, k > 0 ? 1u : 0u);
+          umma_bf16_ts(d, tmem + C::Q_COL + 8 * k, ka + ko, IDESC_S, k > 0 ? 1u : 0u);
         }
       };
-      // O (+)= P[buf] V: 4 K-steps of 16 keys; V is MN-major with its four
-      // 64-column head_dim chunks KV_CHUNK apart.
+      // O (+)= P[buf] V: A = P[buf] in TMEM (4 K-steps of 16 keys), B = V read
+      // MN-major with its four 64-column head_dim chunks KV_CHUNK apart.
       auto issue_PV = [&](int buf, int slot, bool acc) {
-        const uint64_t pa = dP + (uint64_t)((buf * C::P_TILE_BYTES) >> 4);
+        const uint32_t pa = tmem + C::S_COL + buf * C::BN;
         const uint64_t va = dV + (uint64_t)((slot * C::KV_TILE_BYTES) >> 4);
 #pragma unroll
         for (int s = 0; s < C::BN / 16; ++s)
-          umma_bf16_ss(tmem + C::O_COL, pa + (uint64_t)((s * 32) >> 4), va + (uint64_t)((s * 2048) >> 4), IDESC_PV,
+          umma_bf16_ts(tmem + C::O_COL, pa + 8 * s, va + (uint64_t)((s * 2048) >> 4), IDESC_PV,
                        (acc || s > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(&bars->q_full, 0, abort_flag, p.err);
+      bool ok = mbar_wait(&bars->q_tmem, 0, abort_flag, p.err);
       for (int j0 = 0; ok && j0 < min(n, 2); ++j0) {
         const int slot = wait_item();
         if (slot < 0) {
@@ -246,7 +248,31 @@ __global__ void __launch_bounds__(256, 1)
     const float sl2 = p.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
+    if (n > 0) {
+      // Copy this thread's row of Q from the swizzled staging tile into TMEM
+      // (bf16 pairs, 128 columns) for the S MMA's A operand.
+      const bool w = mbar_wait(&bars->q_full, 0, abort_flag, p.err);
+      ok = __all_sync(0xffffffffu, w);
+      if (ok) {
+        const uint32_t qrow = smem_u32(sQ) + row * 128;
+#pragma unroll
+        for (int c = 0; c < C::KCH; ++c) {
+          uint32_t r[32];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint32_t a = qrow + c * C::Q_CHUNK + ((u ^ (row & 7)) << 4);
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(r[4 * u]), "=r"(r[4 * u + 1]), "=r"(r[4 * u + 2]), "=r"(r[4 * u + 3])
+                         : "r"(a));
+          }
+          tmem_st32(tmem + lane_off + C::Q_COL + 32 * c, r);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bars->q_tmem);
+      }
+    }
+    for (int j = 0; ok && j < n; ++j) {
       const int buf = j & 1;
       const bool w = mbar_wait(&bars->s_full[buf], (uint32_t)(j >> 1) & 1u, abort_flag, p.err);
       if (!__all_sync(0xffffffffu, w)) {
@@ -286,11 +312,12 @@ __global__ void __launch_bounds__(256, 1)
         rescale = true;
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      const uint32_t pbase = smem_u32(sP) + buf * C::P_TILE_BYTES;
-      if (lim == C::BN - 1)
-        l_run += softmax_p_row<C::BN, true>(s, sl2, m_use, pbase, C::P_TILE_BYTES, row);
+      const uint32_t tP = tmem + lane_off + C::S_COL + buf * C::BN;
+      // Warp-uniform choice: the TMEM stores inside are warp-wide.
+      if (__all_sync(0xffffffffu, lim == C::BN - 1))
+        l_run += softmax_p_row_tmem<C::BN, true>(s, sl2, m_use, tP);
       else
-        l_run += softmax_p_row<C::BN, false>(s, sl2, m_use, pbase, C::P_TILE_BYTES, row);
+        l_run += softmax_p_row_tmem<C::BN, false>(s, sl2, m_use, tP);
 #undef S_AT
       if (__any_sync(0xffffffffu, rescale)) {
         // O holds blocks up to j-1 once PV(j-1) has completed.
@@ -309,9 +336,8 @@ __global__ void __launch_bounds__(256, 1)
           for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * alpha);
           tmem_st32(tO + 32 * c, o);
         }
-        tmem_wait_st();
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();  // P and any O rescale are in TMEM before the MMA reads them
       tc_fence_before();
       mbar_arrive(&bars->p_full[buf]);
     }

@@ -100,6 +100,39 @@ __device__ __forceinline__ float softmax_p_row(const uint32_t (&s)[BN / 32][32],
   return r2.x + r2.y;
 }
 
+// Same as softmax_p_row, but P goes to tensor memory for an MMA that reads its
+// A operand from TMEM: columns tP .. tP + BN/2 of this thread's lane, two bf16
+// per 32-bit column (even key in the low half). The caller waits for the
+// stores (tcgen05.wait::st) before publishing P. The TMEM stores are
+// warp-collective: every lane of the warp must call this with the same kEmu.
+template <int BN, bool kEmu>
+__device__ __forceinline__ float softmax_p_row_tmem(const uint32_t (&s)[BN / 32][32], float sl2, float m_use,
+                                                    uint32_t tP) {
+  const float2 sc2 = make_float2(sl2, sl2);
+  const float2 nm2 = make_float2(-m_use, -m_use);
+  float2 acc[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) acc[k] = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int q = 0; q < BN / 32; ++q) {
+    uint32_t wv[16];
+#pragma unroll
+    for (int pp = 0; pp < 16; ++pp) {
+      const float2 x = __ffma2_rn(make_float2(u2f(s[q][2 * pp]), u2f(s[q][2 * pp + 1])), sc2, nm2);
+      float2 e;
+      if (kEmu && (pp & 3) < kExp2EmuPairs)
+        e = exp2_fma2(x);
+      else
+        e = make_float2(ex2(x.x), ex2(x.y));
+      acc[pp & 3] = __fadd2_rn(acc[pp & 3], e);
+      wv[pp] = pack_bf16x2(e.x, e.y);
+    }
+    tmem_st16(tP + 16 * q, wv);
+  }
+  const float2 r2 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+  return r2.x + r2.y;
+}
+
 // Scale one 32-column chunk of an output row by inv_l and store it (fp32 or
 // bf16) with 16-byte stores.
 __device__ __forceinline__ void store_out_chunk(const PrefillParams& p, int b, int h, int grow, int c,

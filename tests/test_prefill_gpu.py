@@ -18,13 +18,14 @@ def _rand(shape, gen, dev):
 
 
 def test_umma_layouts(cuda_dev):
-    """One 128^3 tcgen05 MMA per operand layout (K-major B and MN-major B)."""
+    """One 128^3 tcgen05 MMA per operand layout: K-major B, MN-major B, and
+    MN-major B with A read from tensor memory."""
     from npu_b200 import _lib
 
     g = torch.Generator().manual_seed(0)
     a = torch.randn(128, 128, generator=g).bfloat16()
     b = torch.randn(128, 128, generator=g).bfloat16()
-    for mn in (0, 1):
+    for mn in (0, 1, 2):
         c = torch.zeros(128, 128, dtype=torch.float32, device=cuda_dev)
         ad, bd = a.to(cuda_dev), b.to(cuda_dev)
         rc = _lib.load().b2a_diag_umma_gemm(ad.data_ptr(), bd.data_ptr(), c.data_ptr(), mn,
