@@ -60,17 +60,6 @@ def decode_lengths(seed: int = 0) -> list[int]:
     return torch.randint(CFG4["Lmin"], CFG4["Lmax"] + 1, (CFG4["B"],), generator=g).tolist()
 
 
-def shard_decode(lens: list[int], world: int) -> list[list[int]]:
-    """Greedy longest-first bin packing of sequences onto ranks by length."""
-    bins = [[] for _ in range(world)]
-    load = [0] * world
-    for i in sorted(range(len(lens)), key=lambda i: -lens[i]):
-        r = min(range(world), key=lambda r: (load[r], r))
-        bins[r].append(i)
-        load[r] += lens[i]
-    return [sorted(b) for b in bins]
-
-
 class ClockSampler:
     """nvidia-smi sampling during the timed region (200 ms period)."""
 
@@ -300,8 +289,10 @@ def run_ours(a, dist: Dist) -> dict | None:
 def run_decode(a, dist: Dist, dev, pk) -> dict:
     from npu_b200 import api
 
+    from npu_b200.dist import shard_sequences
+
     lens = decode_lengths(0)
-    mine = shard_decode(lens, dist.world)[dist.rank]
+    mine = shard_sequences(lens, dist.world)[dist.rank]
     Bm, Hq, Hkv, D, Lmax = len(mine), CFG4["Hq"], CFG4["Hkv"], CFG4["D"], CFG4["Lmax"]
     g = torch.Generator(device=dev).manual_seed(2000 + dist.rank)
     q = torch.randn(Bm, Hq, D, device=dev, generator=g, dtype=torch.bfloat16)

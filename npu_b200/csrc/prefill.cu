@@ -252,36 +252,54 @@ __global__ void __launch_bounds__(384, 1)
         for (int i = 0; i < C::BN; ++i)
           if (i > lim) s[i >> 5][i & 31] = f2u(-INFINITY);
       }
-      // Row max: four independent chains of 3-input max.
-      float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < C::BN; i += 8) {
-        a0 = fmax3(a0, S_AT(i), S_AT(i + 1));
-        a1 = fmax3(a1, S_AT(i + 2), S_AT(i + 3));
-        a2 = fmax3(a2, S_AT(i + 4), S_AT(i + 5));
-        a3 = fmax3(a3, S_AT(i + 6), S_AT(i + 7));
-      }
-      const float mx = fmaxf(fmax3(a0, a1, a2), a3);
-      const float m_blk = mx * sl2;
-      const float m_new = fmaxf(m_run, m_blk);
+      // The exp2 pipe choice and the fast/slow split must be warp-uniform:
+      // the TMEM stores inside are warp-wide.
+      const bool emu = __all_sync(0xffffffffu, lim == C::BN - 1);
       bool rescale = false;
       float alpha = 1.f;
-      if (j == 0) {
-        m_run = m_new;
-      } else if (m_new > m_run + kRescaleThreshold) {
-        alpha = ex2(m_run - m_new);
-        l_run *= alpha;
-        m_run = m_new;
-        rescale = true;
+      if (__all_sync(0xffffffffu, m_run != -INFINITY)) {
+        // Fast path: P = exp2(S * scale * log2e - m_run) with the running max
+        // of earlier blocks, this block's max tracked on the side. Only if it
+        // exceeds m_run by more than the threshold is the row redone with the
+        // new max (the first pass's P is overwritten before it is published).
+        float smax;
+        float rs = emu ? softmax_p_row_tmem<C::BN, true, true>(s, sl2, m_run, tS, &smax)
+                       : softmax_p_row_tmem<C::BN, false, true>(s, sl2, m_run, tS, &smax);
+        const float m_blk = smax * sl2;
+        const bool jump = m_blk > m_run + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, jump)) {
+          if (jump) {
+            alpha = ex2(m_run - m_blk);
+            l_run *= alpha;
+            m_run = m_blk;
+            rescale = true;
+          }
+          tmem_wait_st();
+          rs = softmax_p_row_tmem<C::BN, false>(s, sl2, m_run, tS);  // rare: MUFU only
+        }
+        l_run += rs;
+      } else {
+        // First block (or a row that has seen no key yet): row max first.
+        float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < C::BN; i += 8) {
+          a0 = fmax3(a0, S_AT(i), S_AT(i + 1));
+          a1 = fmax3(a1, S_AT(i + 2), S_AT(i + 3));
+          a2 = fmax3(a2, S_AT(i + 4), S_AT(i + 5));
+          a3 = fmax3(a3, S_AT(i + 6), S_AT(i + 7));
+        }
+        const float m_new = fmaxf(m_run, fmaxf(fmax3(a0, a1, a2), a3) * sl2);
+        if (j == 0) {
+          m_run = m_new;
+        } else if (m_new > m_run + kRescaleThreshold) {
+          alpha = ex2(m_run - m_new);
+          l_run *= alpha;
+          m_run = m_new;
+          rescale = true;
+        }
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        l_run += softmax_p_row_tmem<C::BN, false>(s, sl2, m_use, tS);  // once per row: MUFU only
       }
-      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-
-      // P = exp2(S * scale * log2e - m), bf16, over the first half of S_t in TMEM.
-      // The pipe choice must be warp-uniform: the stores inside are warp-wide.
-      if (__all_sync(0xffffffffu, lim == C::BN - 1))
-        l_run += softmax_p_row_tmem<C::BN, true>(s, sl2, m_use, tS);
-      else
-        l_run += softmax_p_row_tmem<C::BN, false>(s, sl2, m_use, tS);
 #undef S_AT
 
       // O_t holds the sum through block j-1 (its last PV finished before

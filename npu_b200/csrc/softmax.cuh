@@ -26,7 +26,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 }
 
 #ifndef B2A_EXP2_DEG
-#define B2A_EXP2_DEG 3
+#define B2A_EXP2_DEG 2
 #endif
 static_assert(B2A_EXP2_DEG == 2 || B2A_EXP2_DEG == 3, "exp2 polynomial degree is 2 or 3");
 
@@ -105,19 +105,24 @@ __device__ __forceinline__ float softmax_p_row(const uint32_t (&s)[BN / 32][32],
 // per 32-bit column (even key in the low half). The caller waits for the
 // stores (tcgen05.wait::st) before publishing P. The TMEM stores are
 // warp-collective: every lane of the warp must call this with the same kEmu.
-template <int BN, bool kEmu>
+// With kTrackMax the raw (unscaled) row max of S is accumulated into *smax
+// alongside, so a caller can compute P with a running max from earlier blocks
+// and only redo the row when this block's max turns out to be much larger.
+template <int BN, bool kEmu, bool kTrackMax = false>
 __device__ __forceinline__ float softmax_p_row_tmem(const uint32_t (&s)[BN / 32][32], float sl2, float m_use,
-                                                    uint32_t tP) {
+                                                    uint32_t tP, float* smax = nullptr) {
   const float2 sc2 = make_float2(sl2, sl2);
   const float2 nm2 = make_float2(-m_use, -m_use);
   float2 acc[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) acc[k] = make_float2(0.f, 0.f);
+  float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
   for (int q = 0; q < BN / 32; ++q) {
     uint32_t wv[16];
 #pragma unroll
     for (int pp = 0; pp < 16; ++pp) {
+      if (kTrackMax) mx[pp & 3] = fmax3(mx[pp & 3], u2f(s[q][2 * pp]), u2f(s[q][2 * pp + 1]));
       const float2 x = __ffma2_rn(make_float2(u2f(s[q][2 * pp]), u2f(s[q][2 * pp + 1])), sc2, nm2);
       float2 e;
       if (kEmu && (pp & 3) < kExp2EmuPairs)
@@ -129,6 +134,7 @@ __device__ __forceinline__ float softmax_p_row_tmem(const uint32_t (&s)[BN / 32]
     }
     tmem_st16(tP + 16 * q, wv);
   }
+  if (kTrackMax) *smax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
   const float2 r2 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
   return r2.x + r2.y;
 }
