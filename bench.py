@@ -181,7 +181,7 @@ def run_ours(a, dist: Dist) -> dict | None:
     dev = dist.init()
     pk, pk_src = peaks()
     world, rank = dist.world, dist.rank
-    B, Hq, Hkv, D = CFG3["B"], CFG3["Hq"], CFG3["Hkv"], CFG3["D"]
+    B, Hq, Hkv, D = a.batch, CFG3["Hq"], CFG3["Hkv"], CFG3["D"]
     T = a.T
     scale = 1.0 / math.sqrt(D)
     b_lo, b_hi = rank * B // world, (rank + 1) * B // world
@@ -196,10 +196,13 @@ def run_ours(a, dist: Dist) -> dict | None:
         api.prefill(q, k, v, scale=scale, out=o, out_dtype=torch.bfloat16)
 
     gpus = ",".join(str(i) for i in range(world))
-    sampler = ClockSampler(gpus) if rank == 0 else None
+    sampler = ClockSampler(gpus) if (rank == 0 and "prefill" in a.legs) else None
     if sampler:
         sampler.__enter__()
-    total_ms, per_ms = timed(step, a.steps, a.warmup, dist)
+    if "prefill" in a.legs:
+        total_ms, per_ms = timed(step, a.steps, a.warmup, dist)
+    else:
+        total_ms = per_ms = float("nan")
     if sampler:
         sampler.__exit__(None, None, None)
     flops_all = prefill_flops(B, Hq, D, T)
@@ -211,7 +214,7 @@ def run_ours(a, dist: Dist) -> dict | None:
 
     # End to end: pinned host buffers, H2D of q/k/v and D2H of o every step.
     e2e = None
-    if a.e2e:
+    if a.e2e and "prefill" in a.legs:
         hq = q.cpu().pin_memory()
         hk = k.cpu().pin_memory()
         hv = v.cpu().pin_memory()
@@ -235,7 +238,7 @@ def run_ours(a, dist: Dist) -> dict | None:
     torch.cuda.empty_cache()
 
     sweep = []
-    for Ts in a.sweep:
+    for Ts in (a.sweep if "sweep" in a.legs else []):
         qs = torch.randn(Bl, Hq, Ts, D, device=dev, generator=g, dtype=torch.bfloat16)
         ks = torch.randn(Bl, Hkv, Ts, D, device=dev, generator=g, dtype=torch.bfloat16)
         vs = torch.randn(Bl, Hkv, Ts, D, device=dev, generator=g, dtype=torch.bfloat16)
@@ -249,11 +252,11 @@ def run_ours(a, dist: Dist) -> dict | None:
         del qs, ks, vs, os_
     torch.cuda.empty_cache()
 
-    decode = run_decode(a, dist, dev, pk) if a.decode else None
-    long_ctx = run_long_context(a, dist, dev, pk) if a.long else None
+    decode = run_decode(a, dist, dev, pk) if (a.decode and "decode" in a.legs) else None
+    long_ctx = run_long_context(a, dist, dev, pk) if (a.long and "long" in a.legs) else None
 
     cpu = None
-    if rank == 0 and world == 1 and a.cpu_baseline:
+    if rank == 0 and world == 1 and a.cpu_baseline and "prefill" in a.legs:
         cpu = cpu_prefill_sample(T, a.cpu_units)
 
     if rank != 0:
@@ -291,7 +294,7 @@ def run_decode(a, dist: Dist, dev, pk) -> dict:
 
     from npu_b200.dist import shard_sequences
 
-    lens = decode_lengths(0)
+    lens = decode_lengths(0)[: a.decode_batch]
     mine = shard_sequences(lens, dist.world)[dist.rank]
     Bm, Hq, Hkv, D, Lmax = len(mine), CFG4["Hq"], CFG4["Hkv"], CFG4["D"], CFG4["Lmax"]
     g = torch.Generator(device=dev).manual_seed(2000 + dist.rank)
@@ -309,7 +312,7 @@ def run_decode(a, dist: Dist, dev, pk) -> dict:
 
     total_ms, per_ms = timed(step, a.steps, a.warmup, dist)
     kv_all = sum(lens) * Hkv * D * 2 * 2
-    qo_all = CFG4["B"] * Hq * D * 2 * 2
+    qo_all = len(lens) * Hq * D * 2 * 2
     kv_rank = sum(lens[i] for i in mine) * Hkv * D * 2 * 2 + Bm * Hq * D * 2 * 2
     value = (kv_all + qo_all) * a.steps / (total_ms * 1e-3) / 1e9
     achieved = kv_rank / (per_ms * 1e-3) / 1e9
@@ -322,7 +325,8 @@ def run_decode(a, dist: Dist, dev, pk) -> dict:
             "scaling": "strong", "parallelism": f"dp{dist.world} over sequences (greedy by length)",
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "kernel": "decode_split_kernel<128> + decode_combine_kernel",
-                         "traffic": load_traffic("decode_cfg4", B=Bm), "launch_ms": per_ms}}
+                         "traffic": load_traffic("decode_cfg4", keys=sum(lens[i] for i in mine)),
+                         "launch_ms": per_ms}}
 
 
 def run_long_context(a, dist: Dist, dev, pk) -> dict:
@@ -379,8 +383,11 @@ def load_traffic(key: str, **kw):
         return None
     if not entry:
         return None
-    per_unit = entry.get("bytes_per_batch")
-    return per_unit * kw["B"] if per_unit is not None else entry.get("bytes_per_launch")
+    if "bytes_per_batch" in entry and "B" in kw:
+        return entry["bytes_per_batch"] * kw["B"]
+    if "bytes_per_key" in entry and "keys" in kw:
+        return entry["bytes_per_key"] * kw["keys"]
+    return entry.get("bytes_per_launch")
 
 
 # ----------------------------------------------------------------- CPU arm
@@ -446,6 +453,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--T", type=int, default=8192)
+    ap.add_argument("--batch", type=int, default=CFG3["B"], help="config-3 batch (64; smaller only for profiling)")
+    ap.add_argument("--decode-batch", type=int, default=CFG4["B"], help="config-4 sequences (128)")
+    ap.add_argument("--legs", type=lambda s: set(x for x in s.split(",") if x),
+                    default={"prefill", "sweep", "decode", "long"}, help="subset of prefill,sweep,decode,long")
     ap.add_argument("--sweep", type=lambda s: [int(x) for x in s.split(",") if x], default=[512, 2048])
     ap.add_argument("--no-decode", dest="decode", action="store_false")
     ap.add_argument("--no-long", dest="long", action="store_false")

@@ -92,7 +92,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 4-D tiled load (no multicast) into this CTA's shared memory; completion is
+// 4-D tiled load into this CTA's own shared memory only; completion is
 // signalled as transaction bytes on `bar`.
 __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0,
                                             int c1, int c2, int c3) {
