@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bars->s_full[t], 1);
-      mbar_init(&bars->p_full[t], 128);
+      mbar_init(&bars->p_full[t], 4);  // one arrive per softmax warp
       mbar_init(&bars->o_full[t], 1);
     }
     mbar_init(&bars->drain, 1);
@@ -92,125 +92,125 @@ __global__ void __launch_bounds__(384, 1)
   // budget, so the compiler allocates it against that budget.
   if (warp < 4) {
   setmaxnreg_dec<C::REGS_LOW>();
+  // The producer and the MMA issuer run as whole warps: every lane walks the
+  // loop and waits, one elected lane issues each copy / MMA / commit (the *_w
+  // helpers), which keeps the operands in uniform registers.
   if (n_kv > 0 && warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&bars->q_full, C::NQT * C::Q_TILE_BYTES);
+    mbar_arrive_expect_tx_w(&bars->q_full, C::NQT * C::Q_TILE_BYTES);
 #pragma unroll
-      for (int t = 0; t < C::NQT; ++t)
+    for (int t = 0; t < C::NQT; ++t)
 #pragma unroll
-        for (int c = 0; c < C::KCH; ++c)
-          tma_load_4d(sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, &tm_q, &bars->q_full, c * 64,
-                      q0 + t * C::BM, h, b);
-      int issued = 0;
-      for (int i = 0; i < 2 * n_kv; ++i) {
-        const int slot = i % C::STAGES;
-        const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
-        if (!mbar_wait(&bars->kv_empty[slot], ph ^ 1u, abort_flag, p.err)) break;
-        const int j = i >> 1;
-        const CUtensorMap* m = (i & 1) ? &tm_v : &tm_k;
-        uint8_t* dst = sKV + slot * C::KV_TILE_BYTES;
-        mbar_arrive_expect_tx(&bars->kv_full[slot], C::KV_TILE_BYTES);
+      for (int c = 0; c < C::KCH; ++c)
+        tma_load_4d_w(sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, &tm_q, &bars->q_full, c * 64, q0 + t * C::BM,
+                      h, b);
+    int issued = 0;
+    for (int i = 0; i < 2 * n_kv; ++i) {
+      const int slot = i % C::STAGES;
+      const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->kv_empty[slot], ph ^ 1u, abort_flag, p.err))) break;
+      const int j = i >> 1;
+      const CUtensorMap* m = (i & 1) ? &tm_v : &tm_k;
+      uint8_t* dst = sKV + slot * C::KV_TILE_BYTES;
+      mbar_arrive_expect_tx_w(&bars->kv_full[slot], C::KV_TILE_BYTES);
 #pragma unroll
-        for (int c = 0; c < C::KCH; ++c)
-          tma_load_4d(dst + c * C::CHUNK_BYTES, m, &bars->kv_full[slot], c * 64, j * C::BN, hk, b);
-        issued = i + 1;
-      }
-      if (*abort_flag) {
-        // Let every copy still in flight land before the CTA releases smem.
-        mbar_wait_quiet(&bars->q_full, 0);
-        for (int i = max(0, issued - C::STAGES); i < issued; ++i)
-          mbar_wait_quiet(&bars->kv_full[i % C::STAGES], (uint32_t)(i / C::STAGES) & 1u);
-      }
+      for (int c = 0; c < C::KCH; ++c)
+        tma_load_4d_w(dst + c * C::CHUNK_BYTES, m, &bars->kv_full[slot], c * 64, j * C::BN, hk, b);
+      issued = i + 1;
+    }
+    if (*abort_flag && lane == 0) {
+      // Let every copy still in flight land before the CTA releases smem.
+      mbar_wait_quiet(&bars->q_full, 0);
+      for (int i = max(0, issued - C::STAGES); i < issued; ++i)
+        mbar_wait_quiet(&bars->kv_full[i % C::STAGES], (uint32_t)(i / C::STAGES) & 1u);
     }
   } else if (n_kv > 0 && warp == 1) {
     // ------------------------------------------------------------ UMMA issuer
-    if (lane == 0) {
-      constexpr uint32_t IDESC_S = umma_idesc_bf16(128, C::BN, false);
-      constexpr uint32_t IDESC_PV = umma_idesc_bf16(128, D, true);
-      // Descriptors are built once; stepping through a tile adds the byte
-      // offset >> 4 to the 14-bit start-address field (smem addresses stay
-      // below 256 KB, so the field never carries into the next one).
-      const uint64_t dQ = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
-      const uint64_t dK = make_sdesc_sw128(smem_u32(sKV), 16, 1024);
-      const uint64_t dV = make_sdesc_sw128(smem_u32(sKV), C::CHUNK_BYTES, 1024);
-      // S_t = Q_t K^T: A = Q tile (K-major), B = K tile (K-major); 16-wide K
-      // steps walk 32 bytes inside a 128-byte swizzle row, then the next chunk.
-      auto issue_S = [&](int t, int slot) {
-        const uint64_t qa = dQ + (uint64_t)((t * C::Q_TILE_BYTES) >> 4);
-        const uint64_t ka = dK + (uint64_t)((slot * C::KV_TILE_BYTES) >> 4);
-        const uint32_t d = tmem + C::S_COL + t * C::BN;
+    constexpr uint32_t IDESC_S = umma_idesc_bf16(128, C::BN, false);
+    constexpr uint32_t IDESC_PV = umma_idesc_bf16(128, D, true);
+    // Descriptors are built once; stepping through a tile adds the byte
+    // offset >> 4 to the 14-bit start-address field (smem addresses stay
+    // below 256 KB, so the field never carries into the next one).
+    const uint64_t dQ = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
+    const uint64_t dK = make_sdesc_sw128(smem_u32(sKV), 16, 1024);
+    const uint64_t dV = make_sdesc_sw128(smem_u32(sKV), C::CHUNK_BYTES, 1024);
+    // S_t = Q_t K^T: A = Q tile (K-major), B = K tile (K-major); 16-wide K
+    // steps walk 32 bytes inside a 128-byte swizzle row, then the next chunk.
+    auto issue_S = [&](int t, int slot) {
+      const uint64_t qa = dQ + (uint64_t)((t * C::Q_TILE_BYTES) >> 4);
+      const uint64_t ka = dK + (uint64_t)((slot * C::KV_TILE_BYTES) >> 4);
+      const uint32_t d = tmem + C::S_COL + t * C::BN;
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint64_t off = (uint64_t)(((k >> 2) * C::CHUNK_BYTES + (k & 3) * 32) >> 4);
-          umma_bf16_ss(d, qa + off, ka + off, IDESC_S, k > 0 ? 1u : 0u);
-        }
-      };
-      // O_t (+)= P_t V: A = P_t in TMEM (16 keys = 8 columns per step), B = V
-      // tile read MN-major (head_dim contiguous); a 16-key step is 16 rows =
-      // 2048 bytes, 64-column head_dim chunks sit CHUNK_BYTES apart (LBO of dV).
-      auto issue_PV = [&](int t, int slot, bool acc) {
-        const uint32_t pa = tmem + C::S_COL + t * C::BN;
-        const uint64_t va = dV + (uint64_t)((slot * C::KV_TILE_BYTES) >> 4);
-        const uint32_t d = tmem + C::O_COL + t * D;
+      for (int k = 0; k < D / 16; ++k) {
+        const uint64_t off = (uint64_t)(((k >> 2) * C::CHUNK_BYTES + (k & 3) * 32) >> 4);
+        umma_bf16_ss_w(d, qa + off, ka + off, IDESC_S, k > 0 ? 1u : 0u);
+      }
+    };
+    // O_t (+)= P_t V: A = P_t in TMEM (16 keys = 8 columns per step), B = V
+    // tile read MN-major (head_dim contiguous); a 16-key step is 16 rows =
+    // 2048 bytes, 64-column head_dim chunks sit CHUNK_BYTES apart (LBO of dV).
+    auto issue_PV = [&](int t, int slot, bool acc) {
+      const uint32_t pa = tmem + C::S_COL + t * C::BN;
+      const uint64_t va = dV + (uint64_t)((slot * C::KV_TILE_BYTES) >> 4);
+      const uint32_t d = tmem + C::O_COL + t * D;
 #pragma unroll
-        for (int s = 0; s < C::BN / 16; ++s)
-          umma_bf16_ts(d, pa + 8 * s, va + (uint64_t)((s * 2048) >> 4), IDESC_PV, (acc || s > 0) ? 1u : 0u);
-      };
-      auto wait_load = [&](int i) -> bool {
-        return mbar_wait(&bars->kv_full[i % C::STAGES], (uint32_t)(i / C::STAGES) & 1u, abort_flag, p.err);
-      };
+      for (int s = 0; s < C::BN / 16; ++s)
+        umma_bf16_ts_w(d, pa + 8 * s, va + (uint64_t)((s * 2048) >> 4), IDESC_PV, (acc || s > 0) ? 1u : 0u);
+    };
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.err));
+    };
+    auto wait_load = [&](int i) -> bool {
+      return wait_all(&bars->kv_full[i % C::STAGES], (uint32_t)(i / C::STAGES) & 1u);
+    };
 
-      // Tile 0 runs n0 blocks, tile 1 runs n_kv (n0 <= n_kv): a tile-0 block
-      // that lies entirely above the diagonal is neither computed nor waited on.
-      bool ok = mbar_wait(&bars->q_full, 0, abort_flag, p.err) && wait_load(0);
-      if (ok) {
-        tc_fence_after();
-        if (n0 > 0) {
-          issue_S(0, 0);
-          tc_commit(&bars->s_full[0]);
-        }
-        issue_S(1, 0);
-        tc_commit(&bars->s_full[1]);
-        tc_commit(&bars->kv_empty[0]);
-        for (int j = 0; j < n_kv; ++j) {
-          const int vi = 2 * j + 1;
-          const int vslot = vi % C::STAGES;
-          if (!wait_load(vi)) break;
-          if (j < n0) {
-            if (!mbar_wait(&bars->p_full[0], (uint32_t)j & 1u, abort_flag, p.err)) break;
-            tc_fence_after();
-            issue_PV(0, vslot, j > 0);
-            if (j + 1 == n0) tc_commit(&bars->o_full[0]);
-          }
-          int kslot = 0;
-          if (j + 1 < n_kv) {
-            const int ki = 2 * j + 2;
-            kslot = ki % C::STAGES;
-            if (!wait_load(ki)) break;
-            tc_fence_after();
-            if (j + 1 < n0) {
-              issue_S(0, kslot);
-              tc_commit(&bars->s_full[0]);
-            }
-          }
-          if (!mbar_wait(&bars->p_full[1], (uint32_t)j & 1u, abort_flag, p.err)) break;
+    // Tile 0 runs n0 blocks, tile 1 runs n_kv (n0 <= n_kv): a tile-0 block
+    // that lies entirely above the diagonal is neither computed nor waited on.
+    if (wait_all(&bars->q_full, 0) && wait_load(0)) {
+      tc_fence_after();
+      if (n0 > 0) {
+        issue_S(0, 0);
+        tc_commit_w(&bars->s_full[0]);
+      }
+      issue_S(1, 0);
+      tc_commit_w(&bars->s_full[1]);
+      tc_commit_w(&bars->kv_empty[0]);
+      // Per key block j: the V_j and K_{j+1} tiles are waited for first
+      // (normally long landed; the MMA warp is idle here anyway, waiting for
+      // the softmax), so that nothing but the softmax handoffs sits between
+      // a tile's PV MMAs and its next S MMAs.
+      for (int j = 0; j < n_kv; ++j) {
+        const int vslot = (2 * j + 1) % C::STAGES;
+        const bool has_next = j + 1 < n_kv;
+        const int kslot = (2 * j + 2) % C::STAGES;
+        if (!wait_load(2 * j + 1)) break;
+        if (has_next && !wait_load(2 * j + 2)) break;
+        if (j < n0) {
+          if (!wait_all(&bars->p_full[0], (uint32_t)j & 1u)) break;
           tc_fence_after();
-          issue_PV(1, vslot, j > 0);
-          tc_commit(&bars->kv_empty[vslot]);
-          if (j + 1 == n_kv) {
-            tc_commit(&bars->o_full[1]);
-          } else {
-            issue_S(1, kslot);
-            tc_commit(&bars->s_full[1]);
-            tc_commit(&bars->kv_empty[kslot]);
+          issue_PV(0, vslot, j > 0);
+          if (j + 1 == n0) tc_commit_w(&bars->o_full[0]);
+          if (j + 1 < n0) {
+            issue_S(0, kslot);
+            tc_commit_w(&bars->s_full[0]);
           }
+        }
+        if (!wait_all(&bars->p_full[1], (uint32_t)j & 1u)) break;
+        tc_fence_after();
+        issue_PV(1, vslot, j > 0);
+        tc_commit_w(&bars->kv_empty[vslot]);
+        if (!has_next) {
+          tc_commit_w(&bars->o_full[1]);
+        } else {
+          issue_S(1, kslot);
+          tc_commit_w(&bars->s_full[1]);
+          tc_commit_w(&bars->kv_empty[kslot]);
         }
       }
-      // Every MMA issued above must finish before TMEM is deallocated.
-      tc_commit(&bars->drain);
-      mbar_wait_quiet(&bars->drain, 0);
     }
+    // Every MMA issued above must finish before TMEM is deallocated.
+    tc_commit_w(&bars->drain);
+    mbar_wait_quiet(&bars->drain, 0);
   }
   } else {
     setmaxnreg_inc<C::REGS_HIGH>();
@@ -223,8 +223,8 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t tO = tmem + lane_off + C::O_COL + t * D;
     const int grow = q0 + t * C::BM + row;
     const bool valid = grow < p.Tq;
-    const long long row_pos = (long long)sp + grow;
-    const long long kv_last = p.causal ? min(row_pos, (long long)p.Tk - 1) : (long long)p.Tk - 1;
+    // Last visible key of this row (fits in int: it is below Tk).
+    const int kv_last = p.causal ? (int)min((long long)sp + grow, (long long)p.Tk - 1) : p.Tk - 1;
     const float sl2 = p.scale_log2;
     float m_run = -INFINITY;
     float l_run = 0.f;
@@ -238,34 +238,42 @@ __global__ void __launch_bounds__(384, 1)
         break;
       }
       tc_fence_after();
+      // Keys past the row's last visible key are masked; only blocks that
+      // cross the diagonal (or the end of K) have any. `full` is warp-uniform:
+      // it picks the exp2 pipe split, and the TMEM stores inside the P
+      // routines are warp-wide; full blocks skip the mask pass entirely.
+      const int lim = max(-1, min(C::BN - 1, kv_last - j * C::BN));
+      const bool full = __all_sync(0xffffffffu, lim == C::BN - 1);
+      const bool seen = __all_sync(0xffffffffu, m_run != -INFINITY);
       uint32_t s[4][32];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) tmem_ld32(tS + 32 * q, s[q]);
-      tmem_wait_ld();
-#define S_AT(i) u2f(s[(i) >> 5][(i) & 31])
-
-      // Mask only on blocks that cross this row's last visible key.
-      const long long lim_ll = kv_last - (long long)j * C::BN;
-      const int lim = lim_ll < -1 ? -1 : (lim_ll > C::BN - 1 ? C::BN - 1 : (int)lim_ll);
-      if (lim < C::BN - 1) {
-#pragma unroll
-        for (int i = 0; i < C::BN; ++i)
-          if (i > lim) s[i >> 5][i & 31] = f2u(-INFINITY);
-      }
-      // The exp2 pipe choice and the fast/slow split must be warp-uniform:
-      // the TMEM stores inside are warp-wide.
-      const bool emu = __all_sync(0xffffffffu, lim == C::BN - 1);
       bool rescale = false;
       float alpha = 1.f;
-      if (__all_sync(0xffffffffu, m_run != -INFINITY)) {
-        // Fast path: P = exp2(S * scale * log2e - m_run) with the running max
-        // of earlier blocks, this block's max tracked on the side. Only if it
-        // exceeds m_run by more than the threshold is the row redone with the
-        // new max (the first pass's P is overwritten before it is published).
-        float smax;
-        float rs = emu ? softmax_p_row_tmem<C::BN, true, true>(s, sl2, m_run, tS, &smax)
-                       : softmax_p_row_tmem<C::BN, false, true>(s, sl2, m_run, tS, &smax);
-        const float m_blk = smax * sl2;
+#define S_AT(i) u2f(s[(i) >> 5][(i) & 31])
+      if (full && seen) {
+        // Common case: P = exp2(S * scale * log2e - m_run) with the running
+        // max of earlier blocks, this block's max tracked on the side. The
+        // second half of S is still loading while the first half is done.
+        // Only if the block max exceeds m_run by more than the threshold is
+        // the row redone with the new max (the first pass's P is overwritten
+        // before it is published).
+        tmem_ld32(tS, s[0]);
+        tmem_ld32(tS + 32, s[1]);
+        tmem_wait_ld();
+        tmem_ld32(tS + 64, s[2]);
+        tmem_ld32(tS + 96, s[3]);
+        float2 acc[4];
+        float mx[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          acc[k] = make_float2(0.f, 0.f);
+          mx[k] = -INFINITY;
+        }
+        softmax_p_chunks_tmem<4, 0, 2, true, true>(s, sl2, m_run, tS, acc, mx);
+        tmem_wait_ld();
+        softmax_p_chunks_tmem<4, 2, 2, true, true>(s, sl2, m_run, tS, acc, mx);
+        const float2 r2 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+        float rs = r2.x + r2.y;
+        const float m_blk = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * sl2;
         const bool jump = m_blk > m_run + kRescaleThreshold;
         if (__any_sync(0xffffffffu, jump)) {
           if (jump) {
@@ -279,26 +287,54 @@ __global__ void __launch_bounds__(384, 1)
         }
         l_run += rs;
       } else {
-        // First block (or a row that has seen no key yet): row max first.
-        float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < C::BN; i += 8) {
-          a0 = fmax3(a0, S_AT(i), S_AT(i + 1));
-          a1 = fmax3(a1, S_AT(i + 2), S_AT(i + 3));
-          a2 = fmax3(a2, S_AT(i + 4), S_AT(i + 5));
-          a3 = fmax3(a3, S_AT(i + 6), S_AT(i + 7));
+        for (int q = 0; q < 4; ++q) tmem_ld32(tS + 32 * q, s[q]);
+        tmem_wait_ld();
+        if (!full) {
+#pragma unroll
+          for (int i = 0; i < C::BN; ++i)
+            if (i > lim) s[i >> 5][i & 31] = f2u(-INFINITY);
         }
-        const float m_new = fmaxf(m_run, fmaxf(fmax3(a0, a1, a2), a3) * sl2);
-        if (j == 0) {
-          m_run = m_new;
-        } else if (m_new > m_run + kRescaleThreshold) {
-          alpha = ex2(m_run - m_new);
-          l_run *= alpha;
-          m_run = m_new;
-          rescale = true;
+        if (seen) {
+          // Diagonal block: as above with the exp2 on MUFU only (masked keys
+          // give exact zeros).
+          float smax;
+          float rs = softmax_p_row_tmem<C::BN, false, true>(s, sl2, m_run, tS, &smax);
+          const float m_blk = smax * sl2;
+          const bool jump = m_blk > m_run + kRescaleThreshold;
+          if (__any_sync(0xffffffffu, jump)) {
+            if (jump) {
+              alpha = ex2(m_run - m_blk);
+              l_run *= alpha;
+              m_run = m_blk;
+              rescale = true;
+            }
+            tmem_wait_st();
+            rs = softmax_p_row_tmem<C::BN, false>(s, sl2, m_run, tS);
+          }
+          l_run += rs;
+        } else {
+          // First block (or a row that has seen no key yet): row max first.
+          float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < C::BN; i += 8) {
+            a0 = fmax3(a0, S_AT(i), S_AT(i + 1));
+            a1 = fmax3(a1, S_AT(i + 2), S_AT(i + 3));
+            a2 = fmax3(a2, S_AT(i + 4), S_AT(i + 5));
+            a3 = fmax3(a3, S_AT(i + 6), S_AT(i + 7));
+          }
+          const float m_new = fmaxf(m_run, fmaxf(fmax3(a0, a1, a2), a3) * sl2);
+          if (j == 0) {
+            m_run = m_new;
+          } else if (m_new > m_run + kRescaleThreshold) {
+            alpha = ex2(m_run - m_new);
+            l_run *= alpha;
+            m_run = m_new;
+            rescale = true;
+          }
+          const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+          l_run += softmax_p_row_tmem<C::BN, false>(s, sl2, m_use, tS);  // once per row: MUFU only
         }
-        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        l_run += softmax_p_row_tmem<C::BN, false>(s, sl2, m_use, tS);  // once per row: MUFU only
       }
 #undef S_AT
 
@@ -315,9 +351,12 @@ __global__ void __launch_bounds__(384, 1)
           tmem_st32(tO + 32 * c, o);
         }
       }
-      tmem_wait_st();  // P and any O rescale are in TMEM before the MMA may read them
+      // P and any O rescale are in TMEM before the MMA may read them: every
+      // lane completes its stores and fences, then one arrive per warp.
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars->p_full[t]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[t]);
     }
 
     if (n_mine == 0) {

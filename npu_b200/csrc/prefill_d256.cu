@@ -145,30 +145,34 @@ __global__ void __launch_bounds__(256, 1)
   const uint32_t tmem = bars->tmem_base;
 
   if (warp < 4) {
-    if (n > 0 && warp == 0 && lane == 0) {
+    // Producer and MMA issuer run as whole warps; one elected lane issues
+    // each copy / MMA / commit (the *_w helpers).
+    if (n > 0 && warp == 0) {
       // -------------------------------------------------------- producer
-      mbar_arrive_expect_tx(&bars->q_full, C::Q_BYTES);
+      mbar_arrive_expect_tx_w(&bars->q_full, C::Q_BYTES);
       for (int c = 0; c < C::KCH; ++c)
-        tma_load_4d(sQ + c * C::Q_CHUNK, &tm_q, &bars->q_full, c * 64, q0, h, b);
+        tma_load_4d_w(sQ + c * C::Q_CHUNK, &tm_q, &bars->q_full, c * 64, q0, h, b);
       int issued = 0;
       for (int i = 0; i < n_items; ++i) {
         const int slot = i % C::STAGES;
-        if (!mbar_wait(&bars->kv_empty[slot], ((uint32_t)(i / C::STAGES) & 1u) ^ 1u, abort_flag, p.err)) break;
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait(&bars->kv_empty[slot], ((uint32_t)(i / C::STAGES) & 1u) ^ 1u, abort_flag, p.err)))
+          break;
         int blk;
         const bool is_v = d256_load_item(i, n, &blk);
         uint8_t* dst = sKV + slot * C::KV_TILE_BYTES;
-        mbar_arrive_expect_tx(&bars->kv_full[slot], C::KV_TILE_BYTES);
+        mbar_arrive_expect_tx_w(&bars->kv_full[slot], C::KV_TILE_BYTES);
         for (int c = 0; c < C::KCH; ++c)
-          tma_load_4d(dst + c * C::KV_CHUNK, is_v ? &tm_v : &tm_k, &bars->kv_full[slot], c * 64, blk * C::BN, hk,
+          tma_load_4d_w(dst + c * C::KV_CHUNK, is_v ? &tm_v : &tm_k, &bars->kv_full[slot], c * 64, blk * C::BN, hk,
                       b);
         issued = i + 1;
       }
-      if (*abort_flag) {
+      if (*abort_flag && lane == 0) {
         mbar_wait_quiet(&bars->q_full, 0);
         for (int i = max(0, issued - C::STAGES); i < issued; ++i)
           mbar_wait_quiet(&bars->kv_full[i % C::STAGES], (uint32_t)(i / C::STAGES) & 1u);
       }
-    } else if (n > 0 && warp == 1 && lane == 0) {
+    } else if (n > 0 && warp == 1) {
       // -------------------------------------------------------- UMMA issuer
       constexpr uint32_t IDESC_S = umma_idesc_bf16(128, C::BN, false);
       constexpr uint32_t IDESC_PV = umma_idesc_bf16(128, C::D, true);
@@ -177,7 +181,8 @@ __global__ void __launch_bounds__(256, 1)
       int li = 0;  // next load item to consume
       auto wait_item = [&]() -> int {
         const int slot = li % C::STAGES;
-        const bool ok = mbar_wait(&bars->kv_full[slot], (uint32_t)(li / C::STAGES) & 1u, abort_flag, p.err);
+        const bool ok = __all_sync(
+            0xffffffffu, mbar_wait(&bars->kv_full[slot], (uint32_t)(li / C::STAGES) & 1u, abort_flag, p.err));
         ++li;
         return ok ? slot : -1;
       };
@@ -189,7 +194,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
         for (int k = 0; k < C::D / 16; ++k) {
           const uint64_t ko = (uint64_t)(((k >> 2) * C::KV_CHUNK + (k & 3) * 32) >> 4);
-          umma_bf16_ts(d, tmem + C::Q_COL + 8 * k, ka + ko, IDESC_S, k > 0 ? 1u : 0u);
+          umma_bf16_ts_w(d, tmem + C::Q_COL + 8 * k, ka + ko, IDESC_S, k > 0 ? 1u : 0u);
         }
       };
       // O (+)= P[buf] V: A = P[buf] in TMEM (4 K-steps of 16 keys), B = V read
@@ -199,10 +204,10 @@ __global__ void __launch_bounds__(256, 1)
         const uint64_t va = dV + (uint64_t)((slot * C::KV_TILE_BYTES) >> 4);
 #pragma unroll
         for (int s = 0; s < C::BN / 16; ++s)
-          umma_bf16_ts(tmem + C::O_COL, pa + 8 * s, va + (uint64_t)((s * 2048) >> 4), IDESC_PV,
+          umma_bf16_ts_w(tmem + C::O_COL, pa + 8 * s, va + (uint64_t)((s * 2048) >> 4), IDESC_PV,
                        (acc || s > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(&bars->q_tmem, 0, abort_flag, p.err);
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->q_tmem, 0, abort_flag, p.err));
       for (int j0 = 0; ok && j0 < min(n, 2); ++j0) {
         const int slot = wait_item();
         if (slot < 0) {
@@ -211,28 +216,29 @@ __global__ void __launch_bounds__(256, 1)
         }
         tc_fence_after();
         issue_S(j0, slot);
-        tc_commit(&bars->s_full[j0]);
-        tc_commit(&bars->kv_empty[slot]);
+        tc_commit_w(&bars->s_full[j0]);
+        tc_commit_w(&bars->kv_empty[slot]);
       }
       for (int j = 0; ok && j < n; ++j) {
         const int vslot = wait_item();
         if (vslot < 0) break;
-        if (!mbar_wait(&bars->p_full[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, p.err)) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->p_full[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, p.err)))
+          break;
         tc_fence_after();
         issue_PV(j & 1, vslot, j > 0);
-        tc_commit(&bars->pv_done);
-        tc_commit(&bars->kv_empty[vslot]);
+        tc_commit_w(&bars->pv_done);
+        tc_commit_w(&bars->kv_empty[vslot]);
         if (j + 2 < n) {
           const int kslot = wait_item();
           if (kslot < 0) break;
           tc_fence_after();
           issue_S(j & 1, kslot);
-          tc_commit(&bars->s_full[j & 1]);
-          tc_commit(&bars->kv_empty[kslot]);
+          tc_commit_w(&bars->s_full[j & 1]);
+          tc_commit_w(&bars->kv_empty[kslot]);
         }
       }
-      tc_commit(&bars->o_full);
-      tc_commit(&bars->drain);
+      tc_commit_w(&bars->o_full);
+      tc_commit_w(&bars->drain);
       mbar_wait_quiet(&bars->drain, 0);
     }
   } else {

@@ -108,17 +108,68 @@ __device__ __forceinline__ float softmax_p_row(const uint32_t (&s)[BN / 32][32],
 // With kTrackMax the raw (unscaled) row max of S is accumulated into *smax
 // alongside, so a caller can compute P with a running max from earlier blocks
 // and only redo the row when this block's max turns out to be much larger.
-template <int BN, bool kEmu, bool kTrackMax = false>
+// kLean trades ILP for registers: two partial sums and maxima instead of
+// four, and P stored 8 columns (16 keys) at a time instead of 16.
+template <int BN, bool kEmu, bool kTrackMax = false, bool kLean = false>
 __device__ __forceinline__ float softmax_p_row_tmem(const uint32_t (&s)[BN / 32][32], float sl2, float m_use,
                                                     uint32_t tP, float* smax = nullptr) {
+  constexpr int NACC = kLean ? 2 : 4;
+  constexpr int NST = kLean ? 8 : 16;  // packed columns per TMEM store
   const float2 sc2 = make_float2(sl2, sl2);
   const float2 nm2 = make_float2(-m_use, -m_use);
-  float2 acc[4];
+  float2 acc[NACC];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) acc[k] = make_float2(0.f, 0.f);
-  float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  for (int k = 0; k < NACC; ++k) acc[k] = make_float2(0.f, 0.f);
+  float mx[NACC];
 #pragma unroll
-  for (int q = 0; q < BN / 32; ++q) {
+  for (int k = 0; k < NACC; ++k) mx[k] = -INFINITY;
+#pragma unroll
+  for (int g = 0; g < BN / (2 * NST); ++g) {
+    uint32_t wv[NST];
+#pragma unroll
+    for (int e = 0; e < NST; ++e) {
+      const int pp = g * NST + e;  // column pair index within the row
+      const int q = pp >> 4, i = 2 * (pp & 15);
+      if (kTrackMax) mx[pp % NACC] = fmax3(mx[pp % NACC], u2f(s[q][i]), u2f(s[q][i + 1]));
+      const float2 x = __ffma2_rn(make_float2(u2f(s[q][i]), u2f(s[q][i + 1])), sc2, nm2);
+      float2 e2;
+      if (kEmu && (pp & 3) < kExp2EmuPairs)
+        e2 = exp2_fma2(x);
+      else
+        e2 = make_float2(ex2(x.x), ex2(x.y));
+      acc[pp % NACC] = __fadd2_rn(acc[pp % NACC], e2);
+      wv[e] = pack_bf16x2(e2.x, e2.y);
+    }
+    if constexpr (NST == 8)
+      tmem_st8(tP + NST * g, wv);
+    else
+      tmem_st16(tP + NST * g, wv);
+  }
+  float2 r2 = acc[0];
+#pragma unroll
+  for (int k = 1; k < NACC; ++k) r2 = __fadd2_rn(r2, acc[k]);
+  if (kTrackMax) {
+    float m = mx[0];
+#pragma unroll
+    for (int k = 1; k < NACC; ++k) m = fmaxf(m, mx[k]);
+    *smax = m;
+  }
+  return r2.x + r2.y;
+}
+
+// P for 32-key chunks [Q0, Q0 + NQ) of a row whose S values are in s, with
+// partial row sums and (optionally) raw maxima accumulated into acc / mx.
+// Lets a caller start on the first chunks while TMEM loads of the later ones
+// are still in flight (the P columns written here, tP + 16 q, lie below the
+// S columns of any later chunk). Same pipe split and TMEM store rules as
+// softmax_p_row_tmem.
+template <int NCH, int Q0, int NQ, bool kEmu, bool kTrackMax>
+__device__ __forceinline__ void softmax_p_chunks_tmem(const uint32_t (&s)[NCH][32], float sl2, float m_use,
+                                                      uint32_t tP, float2 (&acc)[4], float (&mx)[4]) {
+  const float2 sc2 = make_float2(sl2, sl2);
+  const float2 nm2 = make_float2(-m_use, -m_use);
+#pragma unroll
+  for (int q = Q0; q < Q0 + NQ; ++q) {
     uint32_t wv[16];
 #pragma unroll
     for (int pp = 0; pp < 16; ++pp) {
@@ -134,9 +185,6 @@ __device__ __forceinline__ float softmax_p_row_tmem(const uint32_t (&s)[BN / 32]
     }
     tmem_st16(tP + 16 * q, wv);
   }
-  if (kTrackMax) *smax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
-  const float2 r2 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
-  return r2.x + r2.y;
 }
 
 // Scale one 32-column chunk of an output row by inv_l and store it (fp32 or
