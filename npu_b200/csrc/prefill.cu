@@ -6,11 +6,6 @@
 
 namespace b2a {
 
-// The running max is only moved (and O rescaled) when the block max exceeds
-// it by more than 2^8 in the exp2 domain; otherwise P values stay <= 256,
-// which bf16 and the fp32 row sum hold exactly enough. This keeps the
-// TMEM round trip for the O rescale off the common path.
-constexpr float kRescaleThreshold = 8.0f;
 
 template <int D>
 __global__ void __launch_bounds__(384, 1)
@@ -62,15 +57,18 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&bars->kv_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->kv_empty[s], 2);  // released by both UMMA issuers
     }
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-      mbar_init(&bars->s_full[t], 1);
-      mbar_init(&bars->p_full[t], 4);  // one arrive per softmax warp
+      mbar_init(&bars->sa_full[t], 1);
+      mbar_init(&bars->sb_full[t], 1);
+      mbar_init(&bars->sb_taken[t], 4);  // one arrive per softmax warp
+      mbar_init(&bars->p_full[t], 4);    // one arrive per softmax warp
       mbar_init(&bars->o_full[t], 1);
     }
-    mbar_init(&bars->drain, 1);
+    mbar_init(&bars->drain[0], 1);
+    mbar_init(&bars->drain[1], 1);
     bars->abort_flag = 0;
     fence_mbar_init();
   }
@@ -124,38 +122,43 @@ __global__ void __launch_bounds__(384, 1)
       for (int i = max(0, issued - C::STAGES); i < issued; ++i)
         mbar_wait_quiet(&bars->kv_full[i % C::STAGES], (uint32_t)(i / C::STAGES) & 1u);
     }
-  } else if (n_kv > 0 && warp == 1) {
-    // ------------------------------------------------------------ UMMA issuer
-    constexpr uint32_t IDESC_S = umma_idesc_bf16(128, C::BN, false);
+  } else if (n_kv > 0 && (warp == 1 || warp == 2)) {
+    // ------------------------------------------------------------ UMMA issuers
+    // Warp 1 issues tile 0's MMAs, warp 2 tile 1's. Both read every K/V
+    // tile they need and release it (kv_empty counts two arrivals).
+    const int t = warp - 1;
+    const int nt = t == 0 ? n0 : n_kv;
+    constexpr uint32_t IDESC_S = umma_idesc_bf16(128, C::HALF, false);
     constexpr uint32_t IDESC_PV = umma_idesc_bf16(128, D, true);
     // Descriptors are built once; stepping through a tile adds the byte
     // offset >> 4 to the 14-bit start-address field (smem addresses stay
     // below 256 KB, so the field never carries into the next one).
-    const uint64_t dQ = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
+    const uint64_t dQ = make_sdesc_sw128(smem_u32(sQ + t * C::Q_TILE_BYTES), 16, 1024);
     const uint64_t dK = make_sdesc_sw128(smem_u32(sKV), 16, 1024);
     const uint64_t dV = make_sdesc_sw128(smem_u32(sKV), C::CHUNK_BYTES, 1024);
-    // S_t = Q_t K^T: A = Q tile (K-major), B = K tile (K-major); 16-wide K
-    // steps walk 32 bytes inside a 128-byte swizzle row, then the next chunk.
-    auto issue_S = [&](int t, int slot) {
-      const uint64_t qa = dQ + (uint64_t)((t * C::Q_TILE_BYTES) >> 4);
-      const uint64_t ka = dK + (uint64_t)((slot * C::KV_TILE_BYTES) >> 4);
-      const uint32_t d = tmem + C::S_COL + t * C::BN;
+    const uint32_t dS = tmem + C::S_COL + t * C::BN;
+    const uint32_t dO = tmem + C::O_COL + t * D;
+    // Half h of S_t = Q_t K^T over keys [64 h, 64 h + 64) of the K tile into
+    // columns [col, col + 64) of R_t: A = Q tile (K-major), B = 64 K rows
+    // (K-major; row 64 starts 8 KB into each 128-row chunk); 16-wide K steps
+    // walk 32 bytes inside a 128-byte swizzle row, then the next chunk.
+    auto issue_S_half = [&](int slot, int h, uint32_t col) {
+      const uint64_t ka = dK + (uint64_t)((slot * C::KV_TILE_BYTES + h * C::HALF * 128) >> 4);
 #pragma unroll
       for (int k = 0; k < D / 16; ++k) {
         const uint64_t off = (uint64_t)(((k >> 2) * C::CHUNK_BYTES + (k & 3) * 32) >> 4);
-        umma_bf16_ss_w(d, qa + off, ka + off, IDESC_S, k > 0 ? 1u : 0u);
+        umma_bf16_ss_w(dS + col, dQ + off, ka + off, IDESC_S, k > 0 ? 1u : 0u);
       }
     };
-    // O_t (+)= P_t V: A = P_t in TMEM (16 keys = 8 columns per step), B = V
-    // tile read MN-major (head_dim contiguous); a 16-key step is 16 rows =
-    // 2048 bytes, 64-column head_dim chunks sit CHUNK_BYTES apart (LBO of dV).
-    auto issue_PV = [&](int t, int slot, bool acc) {
-      const uint32_t pa = tmem + C::S_COL + t * C::BN;
+    // O_t (+)= P_t V: A = P_t in TMEM at columns [pcol, pcol + 64) of R_t
+    // (16 keys = 8 columns per step), B = V tile read MN-major (head_dim
+    // contiguous); a 16-key step is 16 rows = 2048 bytes, 64-column head_dim
+    // chunks sit CHUNK_BYTES apart (LBO of dV).
+    auto issue_PV = [&](int slot, uint32_t pcol, bool acc) {
       const uint64_t va = dV + (uint64_t)((slot * C::KV_TILE_BYTES) >> 4);
-      const uint32_t d = tmem + C::O_COL + t * D;
 #pragma unroll
       for (int s = 0; s < C::BN / 16; ++s)
-        umma_bf16_ts_w(d, pa + 8 * s, va + (uint64_t)((s * 2048) >> 4), IDESC_PV, (acc || s > 0) ? 1u : 0u);
+        umma_bf16_ts_w(dO, dS + pcol + 8 * s, va + (uint64_t)((s * 2048) >> 4), IDESC_PV, (acc || s > 0) ? 1u : 0u);
     };
     auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.err));
@@ -164,53 +167,62 @@ __global__ void __launch_bounds__(384, 1)
       return wait_all(&bars->kv_full[i % C::STAGES], (uint32_t)(i / C::STAGES) & 1u);
     };
 
-    // Tile 0 runs n0 blocks, tile 1 runs n_kv (n0 <= n_kv): a tile-0 block
-    // that lies entirely above the diagonal is neither computed nor waited on.
-    if (wait_all(&bars->q_full, 0) && wait_load(0)) {
-      tc_fence_after();
-      if (n0 > 0) {
-        issue_S(0, 0);
-        tc_commit_w(&bars->s_full[0]);
-      }
-      issue_S(1, 0);
-      tc_commit_w(&bars->s_full[1]);
-      tc_commit_w(&bars->kv_empty[0]);
-      // Per key block j: the V_j and K_{j+1} tiles are waited for first
-      // (normally long landed; the MMA warp is idle here anyway, waiting for
-      // the softmax), so that nothing but the softmax handoffs sits between
-      // a tile's PV MMAs and its next S MMAs.
-      for (int j = 0; j < n_kv; ++j) {
-        const int vslot = (2 * j + 1) % C::STAGES;
-        const bool has_next = j + 1 < n_kv;
-        const int kslot = (2 * j + 2) % C::STAGES;
-        if (!wait_load(2 * j + 1)) break;
-        if (has_next && !wait_load(2 * j + 2)) break;
-        if (j < n0) {
-          if (!wait_all(&bars->p_full[0], (uint32_t)j & 1u)) break;
-          tc_fence_after();
-          issue_PV(0, vslot, j > 0);
-          if (j + 1 == n0) tc_commit_w(&bars->o_full[0]);
-          if (j + 1 < n0) {
-            issue_S(0, kslot);
-            tc_commit_w(&bars->s_full[0]);
-          }
-        }
-        if (!wait_all(&bars->p_full[1], (uint32_t)j & 1u)) break;
+    // Per key block j: once the softmax has taken the second half of S_t(j),
+    // the first half of S_t(j+1) goes into its columns; once P_t(j) is
+    // published, PV_t(j) and then the second half of S_t(j+1) (over P_t(j)'s
+    // columns). V_j and K_{j+1} are waited for first (normally long landed).
+    // K/V load items are K_j = 2 j, V_j = 2 j + 1; `used` counts the items
+    // this warp has released so far, in order.
+    bool ok = wait_all(&bars->q_full, 0);
+    int used = 0;
+    if (ok && nt > 0) {
+      ok = wait_load(0);
+      if (ok) {
         tc_fence_after();
-        issue_PV(1, vslot, j > 0);
-        tc_commit_w(&bars->kv_empty[vslot]);
-        if (!has_next) {
-          tc_commit_w(&bars->o_full[1]);
-        } else {
-          issue_S(1, kslot);
-          tc_commit_w(&bars->s_full[1]);
-          tc_commit_w(&bars->kv_empty[kslot]);
-        }
+        issue_S_half(0, 0, 0);
+        tc_commit_w(&bars->sa_full[t]);
+        issue_S_half(0, 1, C::HALF);
+        tc_commit_w(&bars->sb_full[t]);
+        tc_commit_w(&bars->kv_empty[0]);
+        used = 1;
       }
     }
+    for (int j = 0; ok && j < nt; ++j) {
+      const int vslot = (2 * j + 1) % C::STAGES;
+      const bool next = j + 1 < nt;
+      const int kslot = (2 * j + 2) % C::STAGES;
+      const uint32_t fcol = (j & 1) ? C::HALF : 0;  // P_t(j), then S_t(j+1)'s second half
+      if (!wait_load(2 * j + 1) || (next && !wait_load(2 * j + 2))) break;
+      if (next) {
+        if (!wait_all(&bars->sb_taken[t], (uint32_t)j & 1u)) break;
+        tc_fence_after();
+        issue_S_half(kslot, 0, C::HALF - fcol);
+        tc_commit_w(&bars->sa_full[t]);
+      }
+      if (!wait_all(&bars->p_full[t], (uint32_t)j & 1u)) break;
+      tc_fence_after();
+      issue_PV(vslot, fcol, j > 0);
+      tc_commit_w(&bars->kv_empty[vslot]);
+      if (next) {
+        issue_S_half(kslot, 1, fcol);
+        tc_commit_w(&bars->sb_full[t]);
+        tc_commit_w(&bars->kv_empty[kslot]);
+        used = 2 * j + 3;
+      } else {
+        tc_commit_w(&bars->o_full[t]);
+        used = 2 * j + 2;
+      }
+    }
+    // K/V tiles of blocks this tile never reaches (tile 0 stops one block
+    // short at the diagonal) are released once they have landed: landing
+    // means the slot is in the phase of exactly that tile.
+    for (int i = used; ok && i < 2 * n_kv; ++i) {
+      if (!wait_load(i)) break;
+      if (lane == 0) mbar_arrive(&bars->kv_empty[i % C::STAGES]);
+    }
     // Every MMA issued above must finish before TMEM is deallocated.
-    tc_commit_w(&bars->drain);
-    mbar_wait_quiet(&bars->drain, 0);
+    tc_commit_w(&bars->drain[t]);
+    mbar_wait_quiet(&bars->drain[t], 0);
   }
   } else {
     setmaxnreg_inc<C::REGS_HIGH>();
@@ -219,7 +231,7 @@ __global__ void __launch_bounds__(384, 1)
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-    const uint32_t tS = tmem + lane_off + C::S_COL + t * C::BN;
+    const uint32_t tR = tmem + lane_off + C::S_COL + t * C::BN;  // this row's S/P region
     const uint32_t tO = tmem + lane_off + C::O_COL + t * D;
     const int grow = q0 + t * C::BM + row;
     const bool valid = grow < p.Tq;
@@ -232,114 +244,56 @@ __global__ void __launch_bounds__(384, 1)
     const int n_mine = t == 0 ? n0 : n_kv;
 
     for (int j = 0; j < n_mine; ++j) {
-      const bool w = mbar_wait(&bars->s_full[t], (uint32_t)j & 1u, abort_flag, p.err);
-      if (!__all_sync(0xffffffffu, w)) {
+      const uint32_t fcol = (j & 1) ? C::HALF : 0;  // first half of S_t(j); P_t(j) goes here
+      const uint32_t scol = C::HALF - fcol;         // second half of S_t(j)
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->sa_full[t], (uint32_t)j & 1u, abort_flag, p.err))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      // Keys past the row's last visible key are masked; only blocks that
-      // cross the diagonal (or the end of K) have any. `full` is warp-uniform:
-      // it picks the exp2 pipe split, and the TMEM stores inside the P
-      // routines are warp-wide; full blocks skip the mask pass entirely.
-      const int lim = max(-1, min(C::BN - 1, kv_last - j * C::BN));
-      const bool full = __all_sync(0xffffffffu, lim == C::BN - 1);
-      const bool seen = __all_sync(0xffffffffu, m_run != -INFINITY);
-      uint32_t s[4][32];
-      bool rescale = false;
-      float alpha = 1.f;
-#define S_AT(i) u2f(s[(i) >> 5][(i) & 31])
-      if (full && seen) {
-        // Common case: P = exp2(S * scale * log2e - m_run) with the running
-        // max of earlier blocks, this block's max tracked on the side. The
-        // second half of S is still loading while the first half is done.
-        // Only if the block max exceeds m_run by more than the threshold is
-        // the row redone with the new max (the first pass's P is overwritten
-        // before it is published).
-        tmem_ld32(tS, s[0]);
-        tmem_ld32(tS + 32, s[1]);
-        tmem_wait_ld();
-        tmem_ld32(tS + 64, s[2]);
-        tmem_ld32(tS + 96, s[3]);
-        float2 acc[4];
-        float mx[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          acc[k] = make_float2(0.f, 0.f);
-          mx[k] = -INFINITY;
-        }
-        softmax_p_chunks_tmem<4, 0, 2, true, true>(s, sl2, m_run, tS, acc, mx);
-        tmem_wait_ld();
-        softmax_p_chunks_tmem<4, 2, 2, true, true>(s, sl2, m_run, tS, acc, mx);
-        const float2 r2 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
-        float rs = r2.x + r2.y;
-        const float m_blk = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * sl2;
-        const bool jump = m_blk > m_run + kRescaleThreshold;
-        if (__any_sync(0xffffffffu, jump)) {
-          if (jump) {
-            alpha = ex2(m_run - m_blk);
-            l_run *= alpha;
-            m_run = m_blk;
-            rescale = true;
-          }
-          tmem_wait_st();
-          rs = softmax_p_row_tmem<C::BN, false>(s, sl2, m_run, tS);  // rare: MUFU only
-        }
-        l_run += rs;
-      } else {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) tmem_ld32(tS + 32 * q, s[q]);
-        tmem_wait_ld();
-        if (!full) {
-#pragma unroll
-          for (int i = 0; i < C::BN; ++i)
-            if (i > lim) s[i >> 5][i & 31] = f2u(-INFINITY);
-        }
-        if (seen) {
-          // Diagonal block: as above with the exp2 on MUFU only (masked keys
-          // give exact zeros).
-          float smax;
-          float rs = softmax_p_row_tmem<C::BN, false, true>(s, sl2, m_run, tS, &smax);
-          const float m_blk = smax * sl2;
-          const bool jump = m_blk > m_run + kRescaleThreshold;
-          if (__any_sync(0xffffffffu, jump)) {
-            if (jump) {
-              alpha = ex2(m_run - m_blk);
-              l_run *= alpha;
-              m_run = m_blk;
-              rescale = true;
-            }
-            tmem_wait_st();
-            rs = softmax_p_row_tmem<C::BN, false>(s, sl2, m_run, tS);
-          }
-          l_run += rs;
-        } else {
-          // First block (or a row that has seen no key yet): row max first.
-          float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < C::BN; i += 8) {
-            a0 = fmax3(a0, S_AT(i), S_AT(i + 1));
-            a1 = fmax3(a1, S_AT(i + 2), S_AT(i + 3));
-            a2 = fmax3(a2, S_AT(i + 4), S_AT(i + 5));
-            a3 = fmax3(a3, S_AT(i + 6), S_AT(i + 7));
-          }
-          const float m_new = fmaxf(m_run, fmaxf(fmax3(a0, a1, a2), a3) * sl2);
-          if (j == 0) {
-            m_run = m_new;
-          } else if (m_new > m_run + kRescaleThreshold) {
-            alpha = ex2(m_run - m_new);
-            l_run *= alpha;
-            m_run = m_new;
-            rescale = true;
-          }
-          const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-          l_run += softmax_p_row_tmem<C::BN, false>(s, sl2, m_use, tS);  // once per row: MUFU only
-        }
+      // Keys of block j past the row's last visible key are masked.
+      const int lim = kv_last - j * C::BN;
+      // One 64-key half at a time (64 registers of S): the first half's P
+      // is done while the second half may still be on the tensor core.
+      uint32_t s[2][32];
+      tmem_ld32(tR + fcol, s[0]);
+      tmem_ld32(tR + fcol + 32, s[1]);
+      tmem_wait_ld();
+      float hs0, hs1;
+      const float a0 = softmax_half_tmem(s, lim, sl2, m_run, tR + fcol, hs0);
+      // Second half of S_t(j) into registers; then its columns are released
+      // for the first half of S_t(j+1).
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->sb_full[t], (uint32_t)j & 1u, abort_flag, p.err))) {
+        ok = false;
+        break;
       }
-#undef S_AT
+      tc_fence_after();
+      tmem_ld32(tR + scol, s[0]);
+      tmem_ld32(tR + scol + 32, s[1]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->sb_taken[t]);
+      const float a1 = softmax_half_tmem(s, lim - C::HALF, sl2, m_run, tR + fcol + 32, hs1);
+      if (__any_sync(0xffffffffu, a1 != 1.f)) {
+        // Rare: the second half moved the running max; bring the first
+        // half's P (bf16 pairs in TMEM) to the new max.
+        tmem_wait_st();
+        uint32_t pw[32];
+        tmem_ld32(tR + fcol, pw);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          pw[i] = pack_bf16x2(u2f(pw[i] << 16) * a1, u2f(pw[i] & 0xffff0000u) * a1);
+        tmem_st32(tR + fcol, pw);
+      }
+      l_run = (l_run * a0 + hs0) * a1 + hs1;
+      const float alpha = a0 * a1;
+      const bool rescale = j > 0 && alpha != 1.f;
 
-      // O_t holds the sum through block j-1 (its last PV finished before
-      // S_t(j) did); rescale it before the MMA adds block j.
+      // O_t holds the sum through block j-1 (PV_t(j-1) finished before the
+      // second half of S_t(j), which was issued after it, did); rescale it
+      // before the MMA adds block j.
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {

@@ -13,15 +13,26 @@
 // tiles that ping-pong on the tensor core, so one tile's softmax overlaps the
 // other tile's MMAs. Warp roles (12 warps):
 //   warp 0      TMA producer: Q once, then K_j / V_j tiles through a ring
-//   warp 1      TMEM owner + single-thread UMMA issuer
-//   warps 2-3   idle (keep the softmax warpgroups warpgroup-aligned)
+//   warp 1      TMEM owner + UMMA issuer for tile 0
+//   warp 2      UMMA issuer for tile 1 (each tile's MMAs wait only on that
+//               tile's softmax, so one tile's handoffs never stall the other's)
+//   warp 3      idle (keeps the softmax warpgroups warpgroup-aligned)
 //   warps 4-7   softmax + epilogue for tile 0 (thread = row = TMEM lane)
 //   warps 8-11  softmax + epilogue for tile 1
-// TMEM (512 columns): S_0, S_1 (128 fp32 columns each), O_0, O_1 (D columns).
-// P (bf16) is written by the softmax threads into tensor memory over the first
-// half of its own S columns; the PV UMMA reads its A operand from there, so P
-// never touches shared memory (whose bandwidth, shared by the tensor core's
-// operand reads and the TMA fills, is what bounds this kernel).
+// TMEM (512 columns): a 128-column S/P region per tile (R_t = [128 t,
+// 128 t + 128)) and O_0, O_1 (D columns each). S_t(j) is computed as two
+// 64-key halves (N = 64 UMMAs) into the two 64-column halves of R_t, whose
+// roles alternate with the parity of j: the first half lands in
+// first(j) = 64 * (j & 1), the second in the other half. The softmax writes
+// P_t(j) (bf16, two keys per 32-bit column, 64 columns) over first(j), which
+// the PV UMMA reads as its A operand. As soon as the softmax has read the
+// second half of S_t(j) into registers, the first half of S_t(j+1) can go
+// into it; the second half of S_t(j+1) replaces P_t(j) once PV_t(j) is
+// issued (UMMAs from one thread execute in order). So a tile's softmax can
+// start on block j+1 right after publishing P_t(j), instead of waiting for
+// PV_t(j) and a whole S_t(j+1) to run on the tensor core. P never touches
+// shared memory (whose bandwidth, shared by the tensor core's operand reads
+// and the TMA fills, is the next bound).
 #pragma once
 
 #include "common.cuh"
@@ -58,7 +69,8 @@ struct PrefillCfg {
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
   static constexpr int TMEM_COLS = 512;
-  static constexpr int S_COL = 0;          // S_t at S_COL + t * BN; P_t over its first BN / 2
+  static constexpr int S_COL = 0;          // S/P region R_t at S_COL + t * BN
+  static constexpr int HALF = BN / 2;      // keys per S half (one N = 64 UMMA group)
   static constexpr int O_COL = NQT * BN;   // O_t at O_COL + t * D
   static constexpr int THREADS = 384;
   // setmaxnreg split: warpgroup 0 (TMA + MMA issue) gives registers to the
@@ -78,10 +90,12 @@ struct PrefillBars {
   uint64_t q_full;
   uint64_t kv_full[8];
   uint64_t kv_empty[8];
-  uint64_t s_full[2];
+  uint64_t sa_full[2];   // first 64-key half of S_t(j) is in TMEM
+  uint64_t sb_full[2];   // second half of S_t(j) is in TMEM
+  uint64_t sb_taken[2];  // the softmax has read the second half into registers
   uint64_t p_full[2];
   uint64_t o_full[2];
-  uint64_t drain;
+  uint64_t drain[2];     // per UMMA issuer warp
   uint32_t tmem_base;
   int abort_flag;
 };

@@ -187,6 +187,80 @@ __device__ __forceinline__ void softmax_p_chunks_tmem(const uint32_t (&s)[NCH][3
   }
 }
 
+// The running max of a row is only moved (and everything summed so far
+// rescaled) when a block's max exceeds it by more than 2^8 in the exp2
+// domain; otherwise P values stay <= 256, which bf16 and the fp32 row sum
+// hold exactly enough. This keeps the rescale off the common path.
+constexpr float kRescaleThreshold = 8.0f;
+
+// P for one 64-key half of a row's key block into TMEM columns tP .. tP + 32
+// (two bf16 per column), with the row's running max m_run (exp2 domain).
+// Keys past `lim` (relative to the half's first key) are masked. With a
+// running max present, P is computed with it and the half's max taken
+// alongside; only if that max exceeds m_run by more than the threshold is
+// m_run moved and the half redone (MUFU only). Rows without a running max
+// take the max first. Returns the factor (<= 1) by which everything summed
+// for this row before this half (earlier blocks, the block's earlier half,
+// their P and O) has to be scaled: 1 unless m_run moved. `hsum` receives the
+// half's sum of P. Warp-collective (TMEM stores, votes): all lanes call it.
+__device__ __forceinline__ float softmax_half_tmem(uint32_t (&s)[2][32], int lim, float sl2, float& m_run,
+                                                   uint32_t tP, float& hsum) {
+  const bool full = __all_sync(0xffffffffu, lim >= 63);
+  if (!full) {
+#pragma unroll
+    for (int i = 0; i < 64; ++i)
+      if (i > lim) s[i >> 5][i & 31] = f2u(-INFINITY);
+  }
+  float a = 1.f;
+  float2 acc[4];
+  float mx[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    acc[k] = make_float2(0.f, 0.f);
+    mx[k] = -INFINITY;
+  }
+  if (__all_sync(0xffffffffu, m_run != -INFINITY)) {
+    // exp2 on both pipes only when no key is masked (no -inf inputs).
+    if (full)
+      softmax_p_chunks_tmem<2, 0, 2, true, true>(s, sl2, m_run, tP, acc, mx);
+    else
+      softmax_p_chunks_tmem<2, 0, 2, false, true>(s, sl2, m_run, tP, acc, mx);
+    const float m_blk = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * sl2;
+    const bool jump = m_blk > m_run + kRescaleThreshold;
+    if (__any_sync(0xffffffffu, jump)) {
+      if (jump) {
+        a = ex2(m_run - m_blk);
+        m_run = m_blk;
+      }
+      tmem_wait_st();  // the first pass's stores land before they are overwritten
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[k] = make_float2(0.f, 0.f);
+      softmax_p_chunks_tmem<2, 0, 2, false, false>(s, sl2, m_run, tP, acc, mx);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 64; i += 8) {
+      mx[0] = fmax3(mx[0], u2f(s[i >> 5][(i & 31)]), u2f(s[i >> 5][(i & 31) + 1]));
+      mx[1] = fmax3(mx[1], u2f(s[i >> 5][(i & 31) + 2]), u2f(s[i >> 5][(i & 31) + 3]));
+      mx[2] = fmax3(mx[2], u2f(s[i >> 5][(i & 31) + 4]), u2f(s[i >> 5][(i & 31) + 5]));
+      mx[3] = fmax3(mx[3], u2f(s[i >> 5][(i & 31) + 6]), u2f(s[i >> 5][(i & 31) + 7]));
+    }
+    const float m_new = fmaxf(m_run, fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * sl2);
+    if (m_run == -INFINITY) {
+      if (m_new != -INFINITY) a = 0.f;  // everything before was computed from masked keys: zeros
+      m_run = m_new;
+    } else if (m_new > m_run + kRescaleThreshold) {
+      a = ex2(m_run - m_new);
+      m_run = m_new;
+    }
+    const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+    softmax_p_chunks_tmem<2, 0, 2, false, false>(s, sl2, m_use, tP, acc, mx);
+  }
+  const float2 r2 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+  hsum = r2.x + r2.y;
+  return a;
+}
+
 // Scale one 32-column chunk of an output row by inv_l and store it (fp32 or
 // bf16) with 16-byte stores.
 __device__ __forceinline__ void store_out_chunk(const PrefillParams& p, int b, int h, int grow, int c,

@@ -141,6 +141,30 @@ def test_fully_masked_rows_and_empty_keys(cuda_dev):
     assert torch.all(out == 0)
 
 
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_running_max_jumps(cuda_dev, D):
+    """Scores that climb in steps above the lazy-rescale threshold (2^8 in
+    the exp2 domain) at random keys, so a row's running max moves inside the
+    first and inside the second 64-key half of key blocks: exercises the
+    rescale of P already written for the block and of O."""
+    from npu_b200 import api
+
+    g = torch.Generator().manual_seed(11 + D)
+    B, Hq, Hkv, T = 1, 2, 1, 1024
+    sl2 = math.log2(math.e) / math.sqrt(D)
+    spikes = (torch.rand(T, generator=g) < 1 / 40).float()
+    x = 12.0 * torch.cumsum(spikes, 0) + torch.randn(T, generator=g)  # target S * scale * log2(e)
+    q = torch.ones(B, Hq, T, D).to(torch.bfloat16).to(cuda_dev)
+    k = (x / (D * sl2)).view(1, 1, T, 1).expand(B, Hkv, T, D).to(torch.bfloat16).to(cuda_dev)
+    v = _rand((B, Hkv, T, D), g, cuda_dev)
+    out, lse = api.prefill(q, k, v, return_lse=True)
+    ref = A.dense_attention(q.cpu(), k.cpu(), v.cpu())
+    assert (out.cpu() - ref).abs().max().item() <= TOL
+    s = (q[0].float().cpu() @ A.expand_kv(k.cpu().float(), Hq // Hkv)[0].transpose(-1, -2)) / math.sqrt(D)
+    s = s.masked_fill(A.causal_mask(T, T, 0), float("-inf"))
+    assert (lse[0].cpu() - torch.logsumexp(s, dim=-1)).abs().max().item() < 1e-3 * s.abs().max().item()
+
+
 def test_per_batch_start_positions_and_lse(cuda_dev):
     from npu_b200 import api
 
