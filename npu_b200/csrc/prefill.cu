@@ -64,7 +64,9 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&bars->sa_full[t], 1);
       mbar_init(&bars->sb_full[t], 1);
       mbar_init(&bars->sb_taken[t], 4);  // one arrive per softmax warp
+      mbar_init(&bars->pa_full[t], 4);   // one arrive per softmax warp
       mbar_init(&bars->p_full[t], 4);    // one arrive per softmax warp
+      mbar_init(&bars->pva_done[t], 1);
       mbar_init(&bars->o_full[t], 1);
     }
     mbar_init(&bars->drain[0], 1);
@@ -150,14 +152,15 @@ __global__ void __launch_bounds__(384, 1)
         umma_bf16_ss_w(dS + col, dQ + off, ka + off, IDESC_S, k > 0 ? 1u : 0u);
       }
     };
-    // O_t (+)= P_t V: A = P_t in TMEM at columns [pcol, pcol + 64) of R_t
-    // (16 keys = 8 columns per step), B = V tile read MN-major (head_dim
-    // contiguous); a 16-key step is 16 rows = 2048 bytes, 64-column head_dim
-    // chunks sit CHUNK_BYTES apart (LBO of dV).
-    auto issue_PV = [&](int slot, uint32_t pcol, bool acc) {
+    // O_t (+)= P_t V over keys [64 h, 64 h + 64): A = P_t in TMEM at columns
+    // [pcol + 32 h, pcol + 32 h + 32) of R_t (16 keys = 8 columns per step),
+    // B = V rows of those keys read MN-major (head_dim contiguous); a 16-key
+    // step is 16 rows = 2048 bytes, 64-column head_dim chunks sit CHUNK_BYTES
+    // apart (LBO of dV).
+    auto issue_PV_half = [&](int slot, uint32_t pcol, int h, bool acc) {
       const uint64_t va = dV + (uint64_t)((slot * C::KV_TILE_BYTES) >> 4);
 #pragma unroll
-      for (int s = 0; s < C::BN / 16; ++s)
+      for (int s = 4 * h; s < 4 * h + 4; ++s)
         umma_bf16_ts_w(dO, dS + pcol + 8 * s, va + (uint64_t)((s * 2048) >> 4), IDESC_PV, (acc || s > 0) ? 1u : 0u);
     };
     auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
@@ -199,9 +202,13 @@ __global__ void __launch_bounds__(384, 1)
         issue_S_half(kslot, 0, C::HALF - fcol);
         tc_commit_w(&bars->sa_full[t]);
       }
+      if (!wait_all(&bars->pa_full[t], (uint32_t)j & 1u)) break;
+      tc_fence_after();
+      issue_PV_half(vslot, fcol, 0, j > 0);
+      tc_commit_w(&bars->pva_done[t]);
       if (!wait_all(&bars->p_full[t], (uint32_t)j & 1u)) break;
       tc_fence_after();
-      issue_PV(vslot, fcol, j > 0);
+      issue_PV_half(vslot, fcol, 1, true);
       tc_commit_w(&bars->kv_empty[vslot]);
       if (next) {
         issue_S_half(kslot, 1, fcol);
@@ -261,6 +268,33 @@ __global__ void __launch_bounds__(384, 1)
       tmem_wait_ld();
       float hs0, hs1;
       const float a0 = softmax_half_tmem(s, lim, sl2, m_run, tR + fcol, hs0);
+      auto rescale_O = [&](float f) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + 32 * c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * f);
+          tmem_st32(tO + 32 * c, o);
+        }
+      };
+      if (j > 0 && __any_sync(0xffffffffu, a0 != 1.f)) {
+        // Rare: the running max moved; O (blocks < j) is brought to it before
+        // the first PV half adds block j. PV_t(j-1) is complete once the
+        // second half of S_t(j), issued after it, is.
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->sb_full[t], (uint32_t)j & 1u, abort_flag, p.err))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        rescale_O(a0);
+      }
+      // Publish P for keys 0-63: the first PV half can start now.
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->pa_full[t]);
       // Second half of S_t(j) into registers; then its columns are released
       // for the first half of S_t(j+1).
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->sb_full[t], (uint32_t)j & 1u, abort_flag, p.err))) {
@@ -276,35 +310,18 @@ __global__ void __launch_bounds__(384, 1)
       if (lane == 0) mbar_arrive(&bars->sb_taken[t]);
       const float a1 = softmax_half_tmem(s, lim - C::HALF, sl2, m_run, tR + fcol + 32, hs1);
       if (__any_sync(0xffffffffu, a1 != 1.f)) {
-        // Rare: the second half moved the running max; bring the first
-        // half's P (bf16 pairs in TMEM) to the new max.
-        tmem_wait_st();
-        uint32_t pw[32];
-        tmem_ld32(tR + fcol, pw);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          pw[i] = pack_bf16x2(u2f(pw[i] << 16) * a1, u2f(pw[i] & 0xffff0000u) * a1);
-        tmem_st32(tR + fcol, pw);
+        // Rare: the second half moved the running max. O then holds blocks
+        // < j and the first half of block j (once its PV half completes);
+        // bring it to the new max before the second PV half adds to it.
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->pva_done[t], (uint32_t)j & 1u, abort_flag, p.err))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        rescale_O(a1);
       }
       l_run = (l_run * a0 + hs0) * a1 + hs1;
-      const float alpha = a0 * a1;
-      const bool rescale = j > 0 && alpha != 1.f;
 
-      // O_t holds the sum through block j-1 (PV_t(j-1) finished before the
-      // second half of S_t(j), which was issued after it, did); rescale it
-      // before the MMA adds block j.
-      if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + 32 * c, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * alpha);
-          tmem_st32(tO + 32 * c, o);
-        }
-      }
       // P and any O rescale are in TMEM before the MMA may read them: every
       // lane completes its stores and fences, then one arrive per warp.
       tmem_wait_st();

@@ -30,7 +30,10 @@
 // into it; the second half of S_t(j+1) replaces P_t(j) once PV_t(j) is
 // issued (UMMAs from one thread execute in order). So a tile's softmax can
 // start on block j+1 right after publishing P_t(j), instead of waiting for
-// PV_t(j) and a whole S_t(j+1) to run on the tensor core. P never touches
+// PV_t(j) and a whole S_t(j+1) to run on the tensor core. PV_t(j) itself is
+// issued in two K = 64 halves: the first as soon as P for keys 0-63 is
+// written (mid-block), so only the second half and S_t(j+1)'s second half
+// sit between the end of block j and the middle of block j+1. P never touches
 // shared memory (whose bandwidth, shared by the tensor core's operand reads
 // and the TMA fills, is the next bound).
 #pragma once
@@ -93,6 +96,8 @@ struct PrefillBars {
   uint64_t sa_full[2];   // first 64-key half of S_t(j) is in TMEM
   uint64_t sb_full[2];   // second half of S_t(j) is in TMEM
   uint64_t sb_taken[2];  // the softmax has read the second half into registers
+  uint64_t pa_full[2];   // P_t(j) for the first 64 keys is in TMEM
+  uint64_t pva_done[2];  // the PV MMAs of that first half have completed
   uint64_t p_full[2];
   uint64_t o_full[2];
   uint64_t drain[2];     // per UMMA issuer warp
