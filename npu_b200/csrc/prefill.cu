@@ -196,16 +196,18 @@ __global__ void __launch_bounds__(384, 1)
       const int kslot = (2 * j + 2) % C::STAGES;
       const uint32_t fcol = (j & 1) ? C::HALF : 0;  // P_t(j), then S_t(j+1)'s second half
       if (!wait_load(2 * j + 1) || (next && !wait_load(2 * j + 2))) break;
+      // In the order the softmax produces the events: P for keys 0-63,
+      // the second S half taken, all of P.
+      if (!wait_all(&bars->pa_full[t], (uint32_t)j & 1u)) break;
+      tc_fence_after();
+      issue_PV_half(vslot, fcol, 0, j > 0);
+      tc_commit_w(&bars->pva_done[t]);
       if (next) {
         if (!wait_all(&bars->sb_taken[t], (uint32_t)j & 1u)) break;
         tc_fence_after();
         issue_S_half(kslot, 0, C::HALF - fcol);
         tc_commit_w(&bars->sa_full[t]);
       }
-      if (!wait_all(&bars->pa_full[t], (uint32_t)j & 1u)) break;
-      tc_fence_after();
-      issue_PV_half(vslot, fcol, 0, j > 0);
-      tc_commit_w(&bars->pva_done[t]);
       if (!wait_all(&bars->p_full[t], (uint32_t)j & 1u)) break;
       tc_fence_after();
       issue_PV_half(vslot, fcol, 1, true);
