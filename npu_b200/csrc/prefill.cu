@@ -63,8 +63,7 @@ __global__ void __launch_bounds__(384, 1)
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bars->sa_full[t], 1);
       mbar_init(&bars->sb_full[t], 1);
-      mbar_init(&bars->sb_taken[t], 4);  // one arrive per softmax warp
-      mbar_init(&bars->pa_full[t], 4);   // one arrive per softmax warp
+      mbar_init(&bars->mid[t], 4);       // one arrive per softmax warp
       mbar_init(&bars->p_full[t], 4);    // one arrive per softmax warp
       mbar_init(&bars->pva_done[t], 1);
       mbar_init(&bars->o_full[t], 1);
@@ -196,18 +195,16 @@ __global__ void __launch_bounds__(384, 1)
       const int kslot = (2 * j + 2) % C::STAGES;
       const uint32_t fcol = (j & 1) ? C::HALF : 0;  // P_t(j), then S_t(j+1)'s second half
       if (!wait_load(2 * j + 1) || (next && !wait_load(2 * j + 2))) break;
-      // In the order the softmax produces the events: P for keys 0-63,
-      // the second S half taken, all of P.
-      if (!wait_all(&bars->pa_full[t], (uint32_t)j & 1u)) break;
+      // Mid-block handoff: the next block's first S half (needed first by
+      // the softmax), then the first PV half.
+      if (!wait_all(&bars->mid[t], (uint32_t)j & 1u)) break;
       tc_fence_after();
-      issue_PV_half(vslot, fcol, 0, j > 0);
-      tc_commit_w(&bars->pva_done[t]);
       if (next) {
-        if (!wait_all(&bars->sb_taken[t], (uint32_t)j & 1u)) break;
-        tc_fence_after();
         issue_S_half(kslot, 0, C::HALF - fcol);
         tc_commit_w(&bars->sa_full[t]);
       }
+      issue_PV_half(vslot, fcol, 0, j > 0);
+      tc_commit_w(&bars->pva_done[t]);
       if (!wait_all(&bars->p_full[t], (uint32_t)j & 1u)) break;
       tc_fence_after();
       issue_PV_half(vslot, fcol, 1, true);
@@ -281,35 +278,28 @@ __global__ void __launch_bounds__(384, 1)
           tmem_st32(tO + 32 * c, o);
         }
       };
-      if (j > 0 && __any_sync(0xffffffffu, a0 != 1.f)) {
-        // Rare: the running max moved; O (blocks < j) is brought to it before
-        // the first PV half adds block j. PV_t(j-1) is complete once the
-        // second half of S_t(j), issued after it, is.
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars->sb_full[t], (uint32_t)j & 1u, abort_flag, p.err))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        rescale_O(a0);
-      }
-      // Publish P for keys 0-63: the first PV half can start now.
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->pa_full[t]);
-      // Second half of S_t(j) into registers; then its columns are released
-      // for the first half of S_t(j+1).
+      // Second half of S_t(j) (PV_t(j-1) is complete once it is, since it
+      // was issued after it).
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->sb_full[t], (uint32_t)j & 1u, abort_flag, p.err))) {
         ok = false;
         break;
       }
       tc_fence_after();
+      if (j > 0 && __any_sync(0xffffffffu, a0 != 1.f)) {
+        // Rare: the running max moved; O (blocks < j) is brought to it before
+        // the first PV half adds block j.
+        rescale_O(a0);
+      }
       tmem_ld32(tR + scol, s[0]);
       tmem_ld32(tR + scol + 32, s[1]);
       tmem_wait_ld();
+      // One handoff: P for keys 0-63 is in TMEM (the first PV half can go)
+      // and the second S half is in registers (its columns can take the
+      // first half of S_t(j+1)).
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->sb_taken[t]);
+      if (lane == 0) mbar_arrive(&bars->mid[t]);
       const float a1 = softmax_half_tmem(s, lim - C::HALF, sl2, m_run, tR + fcol + 32, hs1);
       if (__any_sync(0xffffffffu, a1 != 1.f)) {
         // Rare: the second half moved the running max. O then holds blocks

@@ -95,8 +95,8 @@ struct PrefillBars {
   uint64_t kv_empty[8];
   uint64_t sa_full[2];   // first 64-key half of S_t(j) is in TMEM
   uint64_t sb_full[2];   // second half of S_t(j) is in TMEM
-  uint64_t sb_taken[2];  // the softmax has read the second half into registers
-  uint64_t pa_full[2];   // P_t(j) for the first 64 keys is in TMEM
+  uint64_t mid[2];       // P_t(j) for keys 0-63 is in TMEM and the second
+                         // S half has been read into registers
   uint64_t pva_done[2];  // the PV MMAs of that first half have completed
   uint64_t p_full[2];
   uint64_t o_full[2];
