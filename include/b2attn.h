@@ -117,6 +117,31 @@ B2A_API int b2a_decode(const void* q, const void* k_cache, const void* v_cache, 
                const long long* v_strides, const long long* o_strides, float scale, int split_len,
                int out_fp32, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * b2a_prefill / b2a_decode with the gated-attention epilogue of Qwen3.5/3.6
+ * (qwen/forward.py:223-226): the output is attention * sigmoid(gate), fused
+ * into the kernels' output stores (no extra pass over O).
+ *   prefill: gate [B, Hq, Tq, D], element strides gate_strides = {batch,
+ *            head, row}, 16-byte aligned, strides multiples of 16 bytes;
+ *   decode:  gate [B, Hq, D], gate_strides = {batch, head}.
+ * gate_bf16: 1 for bf16, 0 for fp32. The q projection of the reference holds
+ * [q_h | gate_h] per head, so the gate is usually a strided view of it
+ * (head stride 2 D). All other arguments as the ungated calls.
+ */
+B2A_API int b2a_prefill_gated(const void* q, const void* k, const void* v, const void* gate, void* o, float* lse,
+                              int B, int Hq, int Hkv, int Tq, int Tk, int D, const long long* q_strides,
+                              const long long* k_strides, const long long* v_strides,
+                              const long long* gate_strides, const long long* o_strides, int gate_bf16,
+                              int start_pos, const int* start_pos_per_batch, float scale, int causal,
+                              int out_fp32, void* stream);
+
+B2A_API int b2a_decode_gated(const void* q, const void* k_cache, const void* v_cache, const int* seqlens,
+                             const void* gate, void* o, int B, int Hq, int Hkv, int Lmax, int D,
+                             const long long* q_strides, const long long* k_strides, const long long* v_strides,
+                             const long long* gate_strides, const long long* o_strides, int gate_bf16,
+                             float scale, int split_len, int out_fp32, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
 /* Size of the fixed device scratch buffer behind b2a_decode_noalloc. */
 #define B2A_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 
@@ -138,6 +163,65 @@ B2A_API int b2a_decode_noalloc(const void* q, const void* k_cache, const void* v
                                const long long* k_strides, const long long* v_strides,
                                const long long* o_strides, float scale, int split_len, int out_fp32,
                                void* stream);
+
+/*
+ * Fused RoPE + in-place KV-cache append, one launch per layer and step.
+ * Replaces: the per-step projection transposes, the two apply_rope calls,
+ * torch.cat of the layer cache and repeat_interleave of smollm.py:186-208
+ * (and the Tk buckets of smollm.py:17-20,144): the cache is a preallocated
+ * device buffer written in place and read by b2a_prefill / b2a_decode
+ * without expanding GQA heads.
+ *
+ *   q, k, v  [B, T, H, D] views (H = Hq, Hkv, Hkv), element strides
+ *            {batch, token, head} in q/k/v_strides, D contiguous; fp32
+ *            (src_bf16 = 0) or bf16 (src_bf16 = 1); 16-byte aligned, strides
+ *            multiples of 16 bytes
+ *   cos_tab, sin_tab [max_pos, D] contiguous, same dtype as q/k/v: the
+ *            model's rotary tables (build_rope_cache, smollm.py:45-50)
+ *   q_out    [B, Hq, T, D] bf16 contiguous: q rotated (the attention
+ *            kernels' query layout)
+ *   k_cache, v_cache [B, Hkv, Lmax, D] bf16, element strides {batch, head,
+ *            position} in k/v_cache_strides (multiples of 8): rows
+ *            p_b .. p_b + T - 1 receive k rotated and v, where p_b =
+ *            start_pos_per_batch[b] (device int32) or start_pos
+ *   seqlens_out [B] int32 device, optional: set to p_b + T
+ *
+ * Rotation is rotate-half (smollm.py:53-58), computed op by op in the source
+ * dtype as the reference does, then rounded to bf16. Positions must satisfy
+ * 0 <= p_b and p_b + T <= min(Lmax, max_pos): checked on the host for a
+ * scalar start_pos (B2A_ERR_INVALID_ARG), on the device for per-batch
+ * positions (rows out of range are skipped and the device error word reports
+ * B2A_ERR_DEVICE_BAD_LEN). Supported D: 64, 128, 256.
+ */
+B2A_API int b2a_rope_append(const void* q, const void* k, const void* v, const long long* q_strides,
+                            const long long* k_strides, const long long* v_strides, int src_bf16,
+                            const void* cos_tab, const void* sin_tab, int max_pos, void* q_out, void* k_cache,
+                            void* v_cache, const long long* k_cache_strides, const long long* v_cache_strides,
+                            int B, int T, int Hq, int Hkv, int D, int Lmax, int start_pos,
+                            const int* start_pos_per_batch, int* seqlens_out, void* stream);
+
+/*
+ * b2a_rope_append with the gated-attention prologue of Qwen3.5/3.6
+ * (qwen/forward.py:178-204): each q and k head is RMS-normalised over its D
+ * lanes with the weights q_norm / k_norm ([D], source dtype; either may be
+ * null to skip; fp32 statistics, (x * rsqrt(mean(x^2) + eps)) * w as
+ * qwen/forward.py:58-61) and then rotated on its first rope_dim lanes only
+ * (partial rotate-half, qwen/forward.py:81-95; cos_tab/sin_tab are
+ * [max_pos, rope_dim]). rope_dim is 0 (no rotation) or a power of two in
+ * [16, D]. q may be a strided view of the [q_h | gate_h] per-head layout of
+ * the gated q projection (head stride 2 D). Sources need 16-byte alignment
+ * and strides that are multiples of 16 bytes; caches and q_out likewise.
+ * Otherwise as b2a_rope_append (which is this call with rope_dim = D and no
+ * norms).
+ */
+B2A_API int b2a_qk_norm_rope_append(const void* q, const void* k, const void* v, const long long* q_strides,
+                                    const long long* k_strides, const long long* v_strides, int src_bf16,
+                                    const void* q_norm, const void* k_norm, float eps, const void* cos_tab,
+                                    const void* sin_tab, int max_pos, int rope_dim, void* q_out, void* k_cache,
+                                    void* v_cache, const long long* k_cache_strides,
+                                    const long long* v_cache_strides, int B, int T, int Hq, int Hkv, int D,
+                                    int Lmax, int start_pos, const int* start_pos_per_batch, int* seqlens_out,
+                                    void* stream);
 
 /*
  * Read (and optionally clear) the device error word the kernels set on the

@@ -1,4 +1,5 @@
-"""Torch-facing native API over the C ABI: causal GQA prefill and split-KV decode.
+"""Torch-facing native API over the C ABI: causal GQA prefill, split-KV decode
+and the fused RoPE + KV-cache append that feeds them.
 
 These are the B200 entry points behind the reference-compatible wrapper in
 npu_b200.fa (NpuAttention.run_batch). Tensors must already be CUDA bf16 with a
@@ -29,6 +30,15 @@ def _need_cuda_bf16(name: str, t: torch.Tensor, ndim: int) -> None:
         raise ValueError(f"{name} needs a contiguous last (head_dim) dimension")
 
 
+def _check_gate(gate: torch.Tensor, shape: tuple, device: torch.device) -> None:
+    if not isinstance(gate, torch.Tensor) or gate.device != device:
+        raise ValueError("gate must be a CUDA tensor on q's device")
+    if gate.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("gate must be float32 or bfloat16")
+    if tuple(gate.shape) != tuple(shape) or gate.stride(-1) != 1:
+        raise ValueError(f"gate must be {list(shape)} with a contiguous last dim, got {tuple(gate.shape)}")
+
+
 def prefill(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -41,6 +51,7 @@ def prefill(
     out_dtype: torch.dtype = torch.float32,
     out: Optional[torch.Tensor] = None,
     return_lse: bool = False,
+    gate: Optional[torch.Tensor] = None,
 ):
     """Attention forward for q [B, Hq, Tq, D] against k/v [B, Hkv, Tk, D].
 
@@ -49,7 +60,10 @@ def prefill(
     key c is masked iff c > start + r; rows with no key output 0 — the
     semantics of flash_attention_ref (npu/fa_ref.py:42-131). Query head h uses
     KV head h // (Hq // Hkv). Returns o [B, Hq, Tq, D] in out_dtype (and the
-    natural-log LSE [B, Hq, Tq] if return_lse).
+    natural-log LSE [B, Hq, Tq] if return_lse). With `gate` ([B, Hq, Tq, D],
+    fp32 or bf16, any strides with a contiguous last dim) the output is
+    attention * sigmoid(gate), fused into the kernel's stores (Qwen's gated
+    attention, qwen/forward.py:223-226).
     """
     _need_cuda_bf16("q", q, 4)
     _need_cuda_bf16("k", k, 4)
@@ -73,17 +87,32 @@ def prefill(
         if spb.dtype != torch.int32 or spb.device != q.device or spb.numel() != B or not spb.is_contiguous():
             raise ValueError("start_pos_per_batch must be a contiguous int32 tensor [B] on q's device")
     lib = _lib.load()
+    if gate is not None:
+        _check_gate(gate, (B, Hq, Tq, D), q.device)
     with torch.cuda.device(q.device):
-        rc = lib.b2a_prefill(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
-            lse.data_ptr() if lse is not None else None,
-            B, Hq, Hkv, Tq, Tk, D,
-            _lib.ll3(*q.stride()[:3]), _lib.ll3(*k.stride()[:3]), _lib.ll3(*v.stride()[:3]),
-            _lib.ll3(*out.stride()[:3]),
-            int(start_pos), spb.data_ptr() if spb is not None else None,
-            float(scale), 1 if causal else 0, 1 if out_dtype == torch.float32 else 0,
-            _stream_ptr(q.device),
-        )
+        if gate is None:
+            rc = lib.b2a_prefill(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                lse.data_ptr() if lse is not None else None,
+                B, Hq, Hkv, Tq, Tk, D,
+                _lib.ll3(*q.stride()[:3]), _lib.ll3(*k.stride()[:3]), _lib.ll3(*v.stride()[:3]),
+                _lib.ll3(*out.stride()[:3]),
+                int(start_pos), spb.data_ptr() if spb is not None else None,
+                float(scale), 1 if causal else 0, 1 if out_dtype == torch.float32 else 0,
+                _stream_ptr(q.device),
+            )
+        else:
+            rc = lib.b2a_prefill_gated(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), gate.data_ptr(), out.data_ptr(),
+                lse.data_ptr() if lse is not None else None,
+                B, Hq, Hkv, Tq, Tk, D,
+                _lib.ll3(*q.stride()[:3]), _lib.ll3(*k.stride()[:3]), _lib.ll3(*v.stride()[:3]),
+                _lib.ll3(*gate.stride()[:3]), _lib.ll3(*out.stride()[:3]),
+                1 if gate.dtype == torch.bfloat16 else 0,
+                int(start_pos), spb.data_ptr() if spb is not None else None,
+                float(scale), 1 if causal else 0, 1 if out_dtype == torch.float32 else 0,
+                _stream_ptr(q.device),
+            )
     _lib.check(rc, "b2a_prefill")
     return (out, lse) if return_lse else out
 
@@ -103,13 +132,15 @@ def decode(
     split_len: int = 0,
     workspace: Optional[torch.Tensor] = None,
     out: Optional[torch.Tensor] = None,
+    gate: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """One query token per sequence: q [B, Hq, D] against caches [B, Hkv, Lmax, D].
 
     Sequence b attends to keys 0 .. seqlens[b]-1 with no mask (the T=1 path of
     smollm.py:222-234). seqlens is an int32 CUDA tensor [B]. The split-KV
     scratch is taken from `workspace` (a uint8 CUDA tensor) or allocated here
-    through torch's caching allocator.
+    through torch's caching allocator. With `gate` ([B, Hq, D], fp32 or bf16)
+    the output is attention * sigmoid(gate), fused into the combine kernel.
     """
     _need_cuda_bf16("q", q, 3)
     _need_cuda_bf16("k_cache", k_cache, 4)
@@ -133,17 +164,120 @@ def decode(
         workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
     if out is None:
         out = torch.empty((B, Hq, D), dtype=out_dtype, device=q.device)
+    if gate is not None:
+        _check_gate(gate, (B, Hq, D), q.device)
     with torch.cuda.device(q.device):
-        rc = lib.b2a_decode(
-            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), seqlens.data_ptr(), out.data_ptr(),
-            B, Hq, Hkv, Lmax, D,
-            _lib.ll2(*q.stride()[:2]), _lib.ll3(*k_cache.stride()[:3]), _lib.ll3(*v_cache.stride()[:3]),
-            _lib.ll2(*out.stride()[:2]),
-            float(scale), int(split_len), 1 if out.dtype == torch.float32 else 0,
-            workspace.data_ptr(), need, _stream_ptr(q.device),
-        )
+        if gate is None:
+            rc = lib.b2a_decode(
+                q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), seqlens.data_ptr(), out.data_ptr(),
+                B, Hq, Hkv, Lmax, D,
+                _lib.ll2(*q.stride()[:2]), _lib.ll3(*k_cache.stride()[:3]), _lib.ll3(*v_cache.stride()[:3]),
+                _lib.ll2(*out.stride()[:2]),
+                float(scale), int(split_len), 1 if out.dtype == torch.float32 else 0,
+                workspace.data_ptr(), need, _stream_ptr(q.device),
+            )
+        else:
+            rc = lib.b2a_decode_gated(
+                q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), seqlens.data_ptr(), gate.data_ptr(),
+                out.data_ptr(), B, Hq, Hkv, Lmax, D,
+                _lib.ll2(*q.stride()[:2]), _lib.ll3(*k_cache.stride()[:3]), _lib.ll3(*v_cache.stride()[:3]),
+                _lib.ll2(*gate.stride()[:2]), _lib.ll2(*out.stride()[:2]),
+                1 if gate.dtype == torch.bfloat16 else 0,
+                float(scale), int(split_len), 1 if out.dtype == torch.float32 else 0,
+                workspace.data_ptr(), need, _stream_ptr(q.device),
+            )
     _lib.check(rc, "b2a_decode")
     return out
+
+
+def rope_append(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    *,
+    start_pos: int = 0,
+    start_pos_per_batch: Optional[torch.Tensor] = None,
+    seqlens_out: Optional[torch.Tensor] = None,
+    q_out: Optional[torch.Tensor] = None,
+    q_norm: Optional[torch.Tensor] = None,
+    k_norm: Optional[torch.Tensor] = None,
+    norm_eps: float = 1e-6,
+    rope_dim: Optional[int] = None,
+) -> torch.Tensor:
+    """Rotate q and k and append k, v to a device-resident cache, in place.
+
+    q [B, T, Hq, D], k and v [B, T, Hkv, D] (fp32 or bf16, last dim
+    contiguous; typically views of one fused QKV projection) are rotated with
+    the rotary tables cos/sin [max_pos, D] (same dtype, rotate-half form of
+    smollm.py:53-58) at positions p_b + t, p_b = start_pos_per_batch[b] or
+    start_pos. k and v land in rows p_b .. p_b + T - 1 of k_cache/v_cache
+    [B, Hkv, Lmax, D] bf16; seqlens_out (int32 [B], optional) receives
+    p_b + T. Returns q rotated as [B, Hq, T, D] bf16, the layout prefill and
+    decode take.
+
+    Qwen's gated-attention prologue (qwen/forward.py:178-204): q_norm /
+    k_norm ([D], q's dtype) RMS-normalise each q / k head first (eps
+    norm_eps), and rope_dim < D rotates only the first rope_dim lanes (cos/sin
+    are then [max_pos, rope_dim]).
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not t.is_cuda or t.dim() != 4 or t.stride(-1) != 1:
+            raise ValueError(f"{name} must be a CUDA [B, T, H, D] tensor with a contiguous last dim")
+    if q.dtype not in (torch.float32, torch.bfloat16) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("q, k, v must share one dtype, float32 or bfloat16")
+    if cos.dtype != q.dtype or sin.dtype != q.dtype or not cos.is_contiguous() or not sin.is_contiguous():
+        raise ValueError("cos/sin must be contiguous [max_pos, D] tensors in q's dtype")
+    _need_cuda_bf16("k_cache", k_cache, 4)
+    _need_cuda_bf16("v_cache", v_cache, 4)
+    B, T, Hq, D = q.shape
+    Hkv = k.shape[2]
+    Bc, Hc, Lmax, Dc = k_cache.shape
+    if tuple(k.shape) != (B, T, Hkv, D) or tuple(v.shape) != (B, T, Hkv, D):
+        raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
+    if (Bc, Hc, Dc) != (B, Hkv, D) or tuple(v_cache.shape) != tuple(k_cache.shape):
+        raise ValueError(f"cache shape {tuple(k_cache.shape)} does not fit k{tuple(k.shape)}")
+    rope_dim = D if rope_dim is None else int(rope_dim)
+    if cos.dim() != 2 or cos.shape[1] != rope_dim or tuple(sin.shape) != tuple(cos.shape):
+        raise ValueError("cos/sin must be [max_pos, rope_dim]")
+    for name, w in (("q_norm", q_norm), ("k_norm", k_norm)):
+        if w is not None and (w.dtype != q.dtype or w.device != q.device or tuple(w.shape) != (D,)
+                              or not w.is_contiguous()):
+            raise ValueError(f"{name} must be a contiguous [D] tensor in q's dtype on q's device")
+    spb = None
+    if start_pos_per_batch is not None:
+        spb = start_pos_per_batch
+        if spb.dtype != torch.int32 or spb.device != q.device or spb.numel() != B or not spb.is_contiguous():
+            raise ValueError("start_pos_per_batch must be a contiguous int32 tensor [B] on q's device")
+    if seqlens_out is not None:
+        if (seqlens_out.dtype != torch.int32 or seqlens_out.device != q.device or seqlens_out.numel() != B
+                or not seqlens_out.is_contiguous()):
+            raise ValueError("seqlens_out must be a contiguous int32 tensor [B] on q's device")
+    if q_out is None:
+        q_out = torch.empty((B, Hq, T, D), dtype=torch.bfloat16, device=q.device)
+    elif q_out.dtype != torch.bfloat16 or tuple(q_out.shape) != (B, Hq, T, D) or not q_out.is_contiguous():
+        raise ValueError("q_out must be a contiguous bf16 [B, Hq, T, D] tensor")
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        rc = lib.b2a_qk_norm_rope_append(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            _lib.ll3(*q.stride()[:3]), _lib.ll3(*k.stride()[:3]), _lib.ll3(*v.stride()[:3]),
+            1 if q.dtype == torch.bfloat16 else 0,
+            q_norm.data_ptr() if q_norm is not None else None,
+            k_norm.data_ptr() if k_norm is not None else None, float(norm_eps),
+            cos.data_ptr(), sin.data_ptr(), cos.shape[0], rope_dim,
+            q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+            _lib.ll3(*k_cache.stride()[:3]), _lib.ll3(*v_cache.stride()[:3]),
+            B, T, Hq, Hkv, D, Lmax, int(start_pos),
+            spb.data_ptr() if spb is not None else None,
+            seqlens_out.data_ptr() if seqlens_out is not None else None,
+            _stream_ptr(q.device),
+        )
+    _lib.check(rc, "b2a_qk_norm_rope_append")
+    return q_out
 
 
 def device_error(clear: bool = True, device: Optional[torch.device] = None) -> int:

@@ -10,6 +10,7 @@
 #include "b2attn.h"
 #include "decode.cuh"
 #include "prefill.cuh"
+#include "rope_append.cuh"
 
 namespace {
 
@@ -116,32 +117,85 @@ int decode_geometry(int B, int Hq, int Hkv, int D, int Lmax, int split_len, int*
 
 }  // namespace
 
-extern "C" {
+namespace {
 
-const char* b2a_strerror(int code) {
-  switch (code) {
-    case B2A_OK: return "ok";
-    case B2A_ERR_INVALID_ARG: return "invalid argument (null pointer, non-positive size or scale)";
-    case B2A_ERR_HEAD_DIM: return "unsupported head_dim";
-    case B2A_ERR_GQA: return "query heads must be a multiple of KV heads (group <= 16 for decode)";
-    case B2A_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned / innermost stride not 1";
-    case B2A_ERR_TMA: return "TMA tensor map encoding failed";
-    case B2A_ERR_LAUNCH: return "kernel launch failed";
-    case B2A_ERR_WORKSPACE: return "decode workspace missing or too small";
-    case B2A_ERR_DEVICE: return "current CUDA device is not sm_100 (B200)";
-    case B2A_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait ran out (device-side abort)";
-    case B2A_ERR_DEVICE_BAD_LEN: return "a sequence length exceeded the KV cache length";
-    case B2A_ERR_CUDA: return "CUDA runtime error";
-    default: return "unknown b2attn status";
+int rope_append_impl(const void* q, const void* k, const void* v, const long long* qs, const long long* ks,
+                     const long long* vs, int src_bf16, const void* cos_tab, const void* sin_tab, int max_pos,
+                     int rope_dim, const void* q_norm, const void* k_norm, float eps, void* q_out, void* k_cache,
+                     void* v_cache, const long long* kcs, const long long* vcs, int B, int T, int Hq, int Hkv,
+                     int D, int Lmax, int start_pos, const int* start_pos_per_batch, int* seqlens_out,
+                     void* stream) {
+  if (!q || !k || !v || !qs || !ks || !vs || !q_out || !k_cache || !v_cache || !kcs || !vcs)
+    return B2A_ERR_INVALID_ARG;
+  if (B <= 0 || T <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0) return B2A_ERR_INVALID_ARG;
+  if (D != 64 && D != 128 && D != 256) return B2A_ERR_HEAD_DIM;
+  // rope_dim: 0 (no rotation) or a power of two in [16, D] (a rotate-half pair
+  // is then one lane-xor apart in the kernel's layout).
+  if (rope_dim != 0 && (rope_dim < 16 || rope_dim > D || (rope_dim & (rope_dim - 1))))
+    return B2A_ERR_INVALID_ARG;
+  if (rope_dim && (!cos_tab || !sin_tab || max_pos <= 0)) return B2A_ERR_INVALID_ARG;
+  if ((q_norm || k_norm) && !(eps >= 0.f && std::isfinite(eps))) return B2A_ERR_INVALID_ARG;
+  if (!start_pos_per_batch &&
+      (start_pos < 0 || (long long)start_pos + T > Lmax || (rope_dim && (long long)start_pos + T > max_pos)))
+    return B2A_ERR_INVALID_ARG;
+  const uintptr_t src_align = 15u;  // 8 consecutive elements per thread: 32 B (fp32) or 16 B (bf16)
+  for (const void* ptr : {q, k, v, cos_tab, sin_tab, q_norm, k_norm})
+    if (reinterpret_cast<uintptr_t>(ptr) & src_align) return B2A_ERR_ALIGNMENT;
+  for (const void* ptr : {(const void*)q_out, (const void*)k_cache, (const void*)v_cache})
+    if (reinterpret_cast<uintptr_t>(ptr) & 15u) return B2A_ERR_ALIGNMENT;
+  const long long mult = src_bf16 ? 8 : 4;
+  if (!strides_ok(qs, 3, mult) || !strides_ok(ks, 3, mult) || !strides_ok(vs, 3, mult) ||
+      !strides_ok(kcs, 3, 8) || !strides_ok(vcs, 3, 8))
+    return B2A_ERR_ALIGNMENT;
+
+  int* err = nullptr;
+  int rc = prologue(&err);
+  if (rc) return rc;
+  b2a::RopeAppendParams p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  for (int i = 0; i < 3; ++i) {
+    p.qs[i] = qs[i];
+    p.ks[i] = ks[i];
+    p.vs[i] = vs[i];
+    p.kcs[i] = kcs[i];
+    p.vcs[i] = vcs[i];
   }
+  p.cos = cos_tab;
+  p.sin = sin_tab;
+  p.max_pos = max_pos;
+  p.rope_dim = rope_dim;
+  p.q_norm = q_norm;
+  p.k_norm = k_norm;
+  p.norm_eps = eps;
+  p.q_out = q_out;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.B = B;
+  p.T = T;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.D = D;
+  p.Lmax = Lmax;
+  p.start_pos = start_pos;
+  p.start_pos_arr = start_pos_per_batch;
+  p.seqlens_out = seqlens_out;
+  p.src_bf16 = src_bf16 ? 1 : 0;
+  p.err = err;
+  rc = b2a::launch_rope_append(p, static_cast<cudaStream_t>(stream));
+  if (rc == -3) return B2A_ERR_HEAD_DIM;
+  return rc ? B2A_ERR_LAUNCH : B2A_OK;
 }
 
-int b2a_version(void) { return 100; }
+}  // namespace
 
-int b2a_prefill(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv, int Tq,
-                int Tk, int D, const long long* qs, const long long* ks, const long long* vs, const long long* os,
-                int start_pos, const int* start_pos_per_batch, float scale, int causal, int out_fp32,
-                void* stream) {
+namespace {
+
+int prefill_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv, int Tq,
+                 int Tk, int D, const long long* qs, const long long* ks, const long long* vs, const long long* os,
+                 int start_pos, const int* start_pos_per_batch, float scale, int causal, int out_fp32,
+                 const void* gate, const long long* gs, int gate_bf16, void* stream) {
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Tq <= 0 || Tk < 0) return B2A_ERR_INVALID_ARG;
   // With no keys, K and V are never read (every row outputs 0); an empty
   // tensor may come with a null pointer, so give the tensor maps q instead.
@@ -160,6 +214,7 @@ int b2a_prefill(const void* q, const void* k, const void* v, void* o, float* lse
   if (!strides_ok(qs, 3, 8) || !strides_ok(ks, 3, 8) || !strides_ok(vs, 3, 8) ||
       !strides_ok(os, 3, out_fp32 ? 4 : 8))
     return B2A_ERR_ALIGNMENT;
+  if (gate && (!gs || !aligned16(gate) || !strides_ok(gs, 3, gate_bf16 ? 8 : 4))) return B2A_ERR_ALIGNMENT;
   // Query rows per CTA: 256 (two 128-row tiles) for D <= 128, 128 for D = 256.
   const int rows_per_cta = D == 256 ? 128 : 256;
   const long long n_qblk = (Tq + rows_per_cta - 1) / rows_per_cta;
@@ -195,35 +250,23 @@ int b2a_prefill(const void* q, const void* k, const void* v, void* o, float* lse
   p.out_fp32 = out_fp32 ? 1 : 0;
   p.n_qblk = (int)n_qblk;
   p.err = err;
+  p.gate = gate;
+  if (gate) {
+    p.g_sb = gs[0];
+    p.g_sh = gs[1];
+    p.g_st = gs[2];
+    p.gate_bf16 = gate_bf16 ? 1 : 0;
+  }
   rc = D == 256 ? b2a::launch_prefill_d256(tq, tk, tv, p, static_cast<cudaStream_t>(stream))
                : b2a::launch_prefill(D, tq, tk, tv, p, static_cast<cudaStream_t>(stream));
   if (rc == -3) return B2A_ERR_HEAD_DIM;
   return rc ? B2A_ERR_LAUNCH : B2A_OK;
 }
 
-int b2a_decode_default_split(int B, int Hkv, int Lmax) {
-  if (B <= 0 || Hkv <= 0 || Lmax <= 0) return 512;
-  // Aim for ~8 waves of 2 CTAs per SM on 148 SMs assuming an average length of
-  // Lmax / 2, clamped so a split is neither launch-bound nor a long tail.
-  long long want = ((long long)B * Hkv * Lmax) / (2LL * 148 * 2 * 8);
-  want = (want + 63) / 64 * 64;
-  if (want < 512) want = 512;
-  if (want > 4096) want = 4096;
-  return (int)want;
-}
-
-size_t b2a_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int Lmax, int split_len) {
-  if (split_len == 0) split_len = b2a_decode_default_split(B, Hkv, Lmax);
-  int group = 0, max_splits = 0;
-  if (decode_geometry(B, Hq, Hkv, D, Lmax, split_len, &group, &max_splits)) return 0;
-  const size_t n = (size_t)B * Hkv * max_splits * group;
-  return align256(n * D * sizeof(float)) + align256(n * sizeof(float));
-}
-
-int b2a_decode(const void* q, const void* k_cache, const void* v_cache, const int* seqlens, void* o, int B,
-               int Hq, int Hkv, int Lmax, int D, const long long* qs, const long long* ks, const long long* vs,
-               const long long* os, float scale, int split_len, int out_fp32, void* workspace,
-               size_t workspace_bytes, void* stream) {
+int decode_impl(const void* q, const void* k_cache, const void* v_cache, const int* seqlens, void* o, int B,
+                int Hq, int Hkv, int Lmax, int D, const long long* qs, const long long* ks, const long long* vs,
+                const long long* os, float scale, int split_len, int out_fp32, void* workspace,
+                size_t workspace_bytes, const void* gate, const long long* gs, int gate_bf16, void* stream) {
   if (!q || !k_cache || !v_cache || !seqlens || !o || !qs || !ks || !vs || !os) return B2A_ERR_INVALID_ARG;
   if (!(scale > 0.f) || !std::isfinite(scale)) return B2A_ERR_INVALID_ARG;
   if (split_len == 0) split_len = b2a_decode_default_split(B, Hkv, Lmax);
@@ -264,9 +307,119 @@ int b2a_decode(const void* q, const void* k_cache, const void* v_cache, const in
   p.scale_log2 = scale * kLog2e;
   p.out_fp32 = out_fp32 ? 1 : 0;
   p.err = err;
+  p.gate = gate;
+  if (gate) {
+    if (!gs) return B2A_ERR_INVALID_ARG;
+    p.g_sb = gs[0];
+    p.g_sh = gs[1];
+    p.gate_bf16 = gate_bf16 ? 1 : 0;
+  }
   rc = b2a::launch_decode(D, tk, tv, p, static_cast<cudaStream_t>(stream));
   if (rc == -3) return B2A_ERR_HEAD_DIM;
   return rc ? B2A_ERR_LAUNCH : B2A_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* b2a_strerror(int code) {
+  switch (code) {
+    case B2A_OK: return "ok";
+    case B2A_ERR_INVALID_ARG: return "invalid argument (null pointer, non-positive size or scale)";
+    case B2A_ERR_HEAD_DIM: return "unsupported head_dim";
+    case B2A_ERR_GQA: return "query heads must be a multiple of KV heads (group <= 16 for decode)";
+    case B2A_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned / innermost stride not 1";
+    case B2A_ERR_TMA: return "TMA tensor map encoding failed";
+    case B2A_ERR_LAUNCH: return "kernel launch failed";
+    case B2A_ERR_WORKSPACE: return "decode workspace missing or too small";
+    case B2A_ERR_DEVICE: return "current CUDA device is not sm_100 (B200)";
+    case B2A_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait ran out (device-side abort)";
+    case B2A_ERR_DEVICE_BAD_LEN: return "a sequence length exceeded the KV cache length";
+    case B2A_ERR_CUDA: return "CUDA runtime error";
+    default: return "unknown b2attn status";
+  }
+}
+
+int b2a_version(void) { return 100; }
+
+int b2a_decode_default_split(int B, int Hkv, int Lmax) {
+  if (B <= 0 || Hkv <= 0 || Lmax <= 0) return 512;
+  // Aim for ~8 waves of 2 CTAs per SM on 148 SMs assuming an average length of
+  // Lmax / 2, clamped so a split is neither launch-bound nor a long tail.
+  long long want = ((long long)B * Hkv * Lmax) / (2LL * 148 * 2 * 8);
+  want = (want + 63) / 64 * 64;
+  if (want < 512) want = 512;
+  if (want > 4096) want = 4096;
+  return (int)want;
+}
+
+size_t b2a_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int Lmax, int split_len) {
+  if (split_len == 0) split_len = b2a_decode_default_split(B, Hkv, Lmax);
+  int group = 0, max_splits = 0;
+  if (decode_geometry(B, Hq, Hkv, D, Lmax, split_len, &group, &max_splits)) return 0;
+  const size_t n = (size_t)B * Hkv * max_splits * group;
+  return align256(n * D * sizeof(float)) + align256(n * sizeof(float));
+}
+
+int b2a_prefill(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv, int Tq,
+                int Tk, int D, const long long* qs, const long long* ks, const long long* vs, const long long* os,
+                int start_pos, const int* start_pos_per_batch, float scale, int causal, int out_fp32,
+                void* stream) {
+  return prefill_impl(q, k, v, o, lse, B, Hq, Hkv, Tq, Tk, D, qs, ks, vs, os, start_pos, start_pos_per_batch,
+                      scale, causal, out_fp32, nullptr, nullptr, 0, stream);
+}
+
+int b2a_prefill_gated(const void* q, const void* k, const void* v, const void* gate, void* o, float* lse, int B,
+                      int Hq, int Hkv, int Tq, int Tk, int D, const long long* qs, const long long* ks,
+                      const long long* vs, const long long* gs, const long long* os, int gate_bf16,
+                      int start_pos, const int* start_pos_per_batch, float scale, int causal, int out_fp32,
+                      void* stream) {
+  if (!gate || !gs) return B2A_ERR_INVALID_ARG;
+  return prefill_impl(q, k, v, o, lse, B, Hq, Hkv, Tq, Tk, D, qs, ks, vs, os, start_pos, start_pos_per_batch,
+                      scale, causal, out_fp32, gate, gs, gate_bf16, stream);
+}
+
+int b2a_decode(const void* q, const void* k_cache, const void* v_cache, const int* seqlens, void* o, int B,
+               int Hq, int Hkv, int Lmax, int D, const long long* qs, const long long* ks, const long long* vs,
+               const long long* os, float scale, int split_len, int out_fp32, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  return decode_impl(q, k_cache, v_cache, seqlens, o, B, Hq, Hkv, Lmax, D, qs, ks, vs, os, scale, split_len,
+                     out_fp32, workspace, workspace_bytes, nullptr, nullptr, 0, stream);
+}
+
+int b2a_decode_gated(const void* q, const void* k_cache, const void* v_cache, const int* seqlens,
+                     const void* gate, void* o, int B, int Hq, int Hkv, int Lmax, int D, const long long* qs,
+                     const long long* ks, const long long* vs, const long long* gs, const long long* os,
+                     int gate_bf16, float scale, int split_len, int out_fp32, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (!gate || !gs) return B2A_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(gate) & (gate_bf16 ? 1u : 3u)) return B2A_ERR_ALIGNMENT;
+  return decode_impl(q, k_cache, v_cache, seqlens, o, B, Hq, Hkv, Lmax, D, qs, ks, vs, os, scale, split_len,
+                     out_fp32, workspace, workspace_bytes, gate, gs, gate_bf16, stream);
+}
+
+int b2a_rope_append(const void* q, const void* k, const void* v, const long long* qs, const long long* ks,
+                    const long long* vs, int src_bf16, const void* cos_tab, const void* sin_tab, int max_pos,
+                    void* q_out, void* k_cache, void* v_cache, const long long* kcs, const long long* vcs, int B,
+                    int T, int Hq, int Hkv, int D, int Lmax, int start_pos, const int* start_pos_per_batch,
+                    int* seqlens_out, void* stream) {
+  if (!cos_tab || !sin_tab || max_pos <= 0) return B2A_ERR_INVALID_ARG;
+  return rope_append_impl(q, k, v, qs, ks, vs, src_bf16, cos_tab, sin_tab, max_pos, D, nullptr, nullptr, 0.f,
+                          q_out, k_cache, v_cache, kcs, vcs, B, T, Hq, Hkv, D, Lmax, start_pos,
+                          start_pos_per_batch, seqlens_out, stream);
+}
+
+int b2a_qk_norm_rope_append(const void* q, const void* k, const void* v, const long long* qs,
+                            const long long* ks, const long long* vs, int src_bf16, const void* q_norm,
+                            const void* k_norm, float eps, const void* cos_tab, const void* sin_tab,
+                            int max_pos, int rope_dim, void* q_out, void* k_cache, void* v_cache,
+                            const long long* kcs, const long long* vcs, int B, int T, int Hq, int Hkv, int D,
+                            int Lmax, int start_pos, const int* start_pos_per_batch, int* seqlens_out,
+                            void* stream) {
+  return rope_append_impl(q, k, v, qs, ks, vs, src_bf16, cos_tab, sin_tab, max_pos, rope_dim, q_norm, k_norm,
+                          eps, q_out, k_cache, v_cache, kcs, vcs, B, T, Hq, Hkv, D, Lmax, start_pos,
+                          start_pos_per_batch, seqlens_out, stream);
 }
 
 int b2a_get_device_error(int* status, int clear, void* stream) {

@@ -304,7 +304,13 @@ __global__ void decode_combine_kernel(const __grid_constant__ DecodeParams p, in
       wsum += w;
       osum += w * p.part_o[((base + s) * p.group + r) * D + d];
     }
-    const float v = wsum > 0.f ? osum / wsum : 0.f;
+    float v = wsum > 0.f ? osum / wsum : 0.f;
+    if (p.gate) {
+      const long long gi = (long long)b * p.g_sb + (long long)h * p.g_sh + d;
+      const float gv = p.gate_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.gate)[gi])
+                                   : static_cast<const float*>(p.gate)[gi];
+      v *= __fdividef(1.f, 1.f + __expf(-gv));  // sigmoid, as torch.sigmoid in fp32
+    }
     const long long oi = (long long)b * p.o_sb + (long long)h * p.o_sh + d;
     if (p.out_fp32)
       reinterpret_cast<float*>(p.o)[oi] = v;

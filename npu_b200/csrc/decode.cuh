@@ -17,6 +17,11 @@ struct DecodeParams {
   float scale_log2;
   int out_fp32;
   int* err;
+  // Optional output gate [B, Hq, D] (element strides g_sb, g_sh; fp32 or
+  // bf16): o = attention * sigmoid(gate) (qwen/forward.py:223-226).
+  const void* gate;
+  long long g_sb, g_sh;
+  int gate_bf16;
 };
 
 // Launch the split kernel and the LSE combine on `st`. Returns 0 on success,

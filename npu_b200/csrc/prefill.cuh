@@ -54,6 +54,12 @@ struct PrefillParams {
   int out_fp32;
   int n_qblk;          // ceil(Tq / 256)
   int* err;            // device error word (may be nullptr)
+  // Optional output gate [B, Hq, Tq, D] (element strides g_sb, g_sh, g_st,
+  // innermost 1; fp32 or bf16): o = attention * sigmoid(gate), the gated
+  // attention epilogue of qwen/forward.py:223-226. nullptr = no gate.
+  const void* gate;
+  long long g_sb, g_sh, g_st;
+  int gate_bf16;
 };
 
 template <int D>

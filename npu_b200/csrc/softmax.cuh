@@ -261,27 +261,56 @@ __device__ __forceinline__ float softmax_half_tmem(uint32_t (&s)[2][32], int lim
   return a;
 }
 
-// Scale one 32-column chunk of an output row by inv_l and store it (fp32 or
-// bf16) with 16-byte stores.
+// sigmoid(g) = 1 / (1 + e^-g) in fp32 (torch.sigmoid, qwen/forward.py:226).
+__device__ __forceinline__ float sigmoidf_(float g) { return __fdividef(1.f, 1.f + __expf(-g)); }
+
+// Scale one 32-column chunk of an output row by inv_l (and, with a gate, by
+// sigmoid(gate)) and store it (fp32 or bf16) with 16-byte stores.
 __device__ __forceinline__ void store_out_chunk(const PrefillParams& p, int b, int h, int grow, int c,
                                                 const uint32_t (&o)[32], float inv_l) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = u2f(o[i]) * inv_l;
+  if (p.gate) {
+    const long long gi = (long long)b * p.g_sb + (long long)h * p.g_sh + (long long)grow * p.g_st + 32 * c;
+    if (p.gate_bf16) {
+      const uint4* g4 = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.gate) + gi);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 w = g4[i];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          v[8 * i + 2 * k] *= sigmoidf_(u2f(ws[k] << 16));
+          v[8 * i + 2 * k + 1] *= sigmoidf_(u2f(ws[k] & 0xffff0000u));
+        }
+      }
+    } else {
+      const float4* g4 = reinterpret_cast<const float4*>(static_cast<const float*>(p.gate) + gi);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 w = g4[i];
+        v[4 * i] *= sigmoidf_(w.x);
+        v[4 * i + 1] *= sigmoidf_(w.y);
+        v[4 * i + 2] *= sigmoidf_(w.z);
+        v[4 * i + 3] *= sigmoidf_(w.w);
+      }
+    }
+  }
   const long long base = (long long)b * p.o_sb + (long long)h * p.o_sh + (long long)grow * p.o_st + 32 * c;
   if (p.out_fp32) {
     float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.o) + base);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      dst[i] = make_float4(u2f(o[4 * i]) * inv_l, u2f(o[4 * i + 1]) * inv_l, u2f(o[4 * i + 2]) * inv_l,
-                           u2f(o[4 * i + 3]) * inv_l);
-    }
+    for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
   } else {
     uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.o) + base);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint4 w;
-      w.x = pack_bf16x2(u2f(o[8 * i + 0]) * inv_l, u2f(o[8 * i + 1]) * inv_l);
-      w.y = pack_bf16x2(u2f(o[8 * i + 2]) * inv_l, u2f(o[8 * i + 3]) * inv_l);
-      w.z = pack_bf16x2(u2f(o[8 * i + 4]) * inv_l, u2f(o[8 * i + 5]) * inv_l);
-      w.w = pack_bf16x2(u2f(o[8 * i + 6]) * inv_l, u2f(o[8 * i + 7]) * inv_l);
+      w.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
+      w.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
+      w.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
+      w.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
       dst[i] = w;
     }
   }

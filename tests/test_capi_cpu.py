@@ -127,3 +127,53 @@ def test_python_api_refuses_cpu_tensors():
 def test_b2a_error_carries_status_text():
     err = _lib.B2AError(_lib.B2A_ERR_GQA, "b2a_prefill")
     assert err.code == _lib.B2A_ERR_GQA and "multiple" in str(err)
+
+
+def _rope(**over):
+    a = dict(q=FAKE, k=FAKE, v=FAKE, qs=(5 * 8 * 64, 8 * 64, 64), ks=(5 * 2 * 64, 2 * 64, 64),
+             vs=(5 * 2 * 64, 2 * 64, 64), bf16=0, cos=FAKE, sin=FAKE, max_pos=64, q_out=FAKE, kc=FAKE, vc=FAKE,
+             kcs=(2 * 32 * 64, 32 * 64, 64), vcs=(2 * 32 * 64, 32 * 64, 64), B=1, T=5, Hq=8, Hkv=2, D=64,
+             Lmax=32, sp=0, spb=None, seq=None)
+    a.update(over)
+    return _lib.load().b2a_rope_append(
+        a["q"], a["k"], a["v"], _lib.ll3(*a["qs"]), _lib.ll3(*a["ks"]), _lib.ll3(*a["vs"]), a["bf16"], a["cos"],
+        a["sin"], a["max_pos"], a["q_out"], a["kc"], a["vc"], _lib.ll3(*a["kcs"]), _lib.ll3(*a["vcs"]), a["B"],
+        a["T"], a["Hq"], a["Hkv"], a["D"], a["Lmax"], a["sp"], a["spb"], a["seq"], None)
+
+
+def test_rope_append_argument_validation():
+    assert _rope(q=None) == _lib.B2A_ERR_INVALID_ARG
+    assert _rope(T=0) == _lib.B2A_ERR_INVALID_ARG
+    assert _rope(D=96) == _lib.B2A_ERR_HEAD_DIM
+    assert _rope(sp=28) == _lib.B2A_ERR_INVALID_ARG       # 28 + 5 > Lmax
+    assert _rope(sp=-1) == _lib.B2A_ERR_INVALID_ARG
+    assert _rope(max_pos=4) == _lib.B2A_ERR_INVALID_ARG   # positions past the rotary table
+    assert _rope(q=FAKE + 8) == _lib.B2A_ERR_ALIGNMENT    # fp32 sources need 16-byte alignment
+    assert _rope(bf16=1, qs=(5 * 8 * 64, 8 * 64, 68)) == _lib.B2A_ERR_ALIGNMENT  # bf16: 16-byte strides
+    assert _rope(kcs=(2 * 32 * 64, 32 * 64, 66)) == _lib.B2A_ERR_ALIGNMENT
+    assert _rope(kc=FAKE + 4) == _lib.B2A_ERR_ALIGNMENT
+
+
+def _qk_rope(**over):
+    a = dict(q=FAKE, k=FAKE, v=FAKE, qs=(5 * 16 * 512, 16 * 512, 512), ks=(5 * 2 * 256, 2 * 256, 256),
+             vs=(5 * 2 * 256, 2 * 256, 256), bf16=0, qn=FAKE, kn=FAKE, eps=1e-6, cos=FAKE, sin=FAKE, max_pos=64,
+             rd=64, q_out=FAKE, kc=FAKE, vc=FAKE, kcs=(2 * 32 * 256, 32 * 256, 256), vcs=(2 * 32 * 256, 32 * 256, 256),
+             B=1, T=5, Hq=16, Hkv=2, D=256, Lmax=32, sp=0, spb=None, seq=None)
+    a.update(over)
+    return _lib.load().b2a_qk_norm_rope_append(
+        a["q"], a["k"], a["v"], _lib.ll3(*a["qs"]), _lib.ll3(*a["ks"]), _lib.ll3(*a["vs"]), a["bf16"], a["qn"],
+        a["kn"], a["eps"], a["cos"], a["sin"], a["max_pos"], a["rd"], a["q_out"], a["kc"], a["vc"],
+        _lib.ll3(*a["kcs"]), _lib.ll3(*a["vcs"]), a["B"], a["T"], a["Hq"], a["Hkv"], a["D"], a["Lmax"], a["sp"],
+        a["spb"], a["seq"], None)
+
+
+def test_qk_norm_rope_append_argument_validation():
+    assert _qk_rope(rd=48) == _lib.B2A_ERR_INVALID_ARG      # not a power of two
+    assert _qk_rope(rd=8) == _lib.B2A_ERR_INVALID_ARG       # below 16
+    assert _qk_rope(rd=512) == _lib.B2A_ERR_INVALID_ARG     # above D
+    assert _qk_rope(eps=float("nan")) == _lib.B2A_ERR_INVALID_ARG
+    assert _qk_rope(qn=FAKE + 4) == _lib.B2A_ERR_ALIGNMENT
+    assert _qk_rope(rd=0, cos=None, sin=None, sp=40) == _lib.B2A_ERR_INVALID_ARG   # past Lmax
+    if not torch.cuda.is_available():
+        assert _qk_rope() in (_lib.B2A_ERR_CUDA, _lib.B2A_ERR_DEVICE)
+        assert _qk_rope(rd=0, cos=None, sin=None, qn=None, kn=None) in (_lib.B2A_ERR_CUDA, _lib.B2A_ERR_DEVICE)

@@ -1,0 +1,98 @@
+"""Fused RoPE + in-place KV-cache append (b2a_rope_append) and the SmolLM
+forward that runs on it (npu_b200.smollm_b200), against the reference's
+per-step apply_rope + torch.cat path (smollm.py:186-208) restated in
+oracle/smollm_ref.py."""
+import pytest
+import torch
+
+from oracle.smollm_ref import Config, SmolLM, make_state_dict, rope, rope_tables
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rope_append_bit_exact(cuda_dev, D, dtype):
+    from npu_b200 import api
+
+    g = torch.Generator().manual_seed(D)
+    B, T, Hq, Hkv, Lmax, max_pos = 3, 5, 6, 2, 40, 64
+    qkv = torch.randn(B, T, (Hq + 2 * Hkv) * D, generator=g).to(dtype)  # one fused projection output
+    q = qkv[..., :Hq * D].view(B, T, Hq, D)
+    k = qkv[..., Hq * D:(Hq + Hkv) * D].view(B, T, Hkv, D)
+    v = qkv[..., (Hq + Hkv) * D:].view(B, T, Hkv, D)
+    cos, sin = rope_tables(D, max_pos, 10000.0, dtype, "cpu")
+    starts = [0, 7, 35]
+    kc = torch.zeros(B, Hkv, Lmax, D, dtype=torch.bfloat16, device=cuda_dev)
+    vc = torch.zeros_like(kc)
+    seq = torch.full((B,), -1, dtype=torch.int32, device=cuda_dev)
+    spb = torch.tensor(starts, dtype=torch.int32, device=cuda_dev)
+    qd = qkv.to(cuda_dev)
+    q_out = api.rope_append(qd[..., :Hq * D].view(B, T, Hq, D), qd[..., Hq * D:(Hq + Hkv) * D].view(B, T, Hkv, D),
+                            qd[..., (Hq + Hkv) * D:].view(B, T, Hkv, D), cos.to(cuda_dev), sin.to(cuda_dev),
+                            kc, vc, start_pos_per_batch=spb, seqlens_out=seq)
+    assert api.device_error() == 0
+    assert seq.tolist() == [s + T for s in starts]
+    kc, vc, q_out = kc.cpu(), vc.cpu(), q_out.cpu()
+    for b, s in enumerate(starts):
+        cs, sn = cos[s:s + T], sin[s:s + T]
+        ref_q = rope(q[b].transpose(0, 1), cs, sn).to(torch.bfloat16)     # [Hq, T, D]
+        ref_k = rope(k[b].transpose(0, 1), cs, sn).to(torch.bfloat16)
+        assert torch.equal(q_out[b], ref_q)
+        assert torch.equal(kc[b, :, s:s + T], ref_k)
+        assert torch.equal(vc[b, :, s:s + T], v[b].transpose(0, 1).to(torch.bfloat16))
+        untouched = torch.ones(Lmax, dtype=torch.bool)
+        untouched[s:s + T] = False
+        assert torch.all(kc[b, :, untouched] == 0) and torch.all(vc[b, :, untouched] == 0)
+
+
+def test_rope_append_position_checks(cuda_dev):
+    from npu_b200 import api, _lib
+
+    B, T, H, D, Lmax = 2, 4, 2, 64, 16
+    x = torch.randn(B, T, H, D, device=cuda_dev)
+    cos, sin = rope_tables(D, 32, 10000.0, torch.float32, cuda_dev)
+    kc = torch.zeros(B, H, Lmax, D, dtype=torch.bfloat16, device=cuda_dev)
+    vc = torch.zeros_like(kc)
+    with pytest.raises(_lib.B2AError):
+        api.rope_append(x, x, x, cos, sin, kc, vc, start_pos=Lmax - T + 1)  # host-checked
+    api.device_error()
+    spb = torch.tensor([0, Lmax - T + 1], dtype=torch.int32, device=cuda_dev)  # device-checked
+    api.rope_append(x, x, x, cos, sin, kc, vc, start_pos_per_batch=spb)
+    assert api.device_error() == _lib.B2A_ERR_DEVICE_BAD_LEN
+    # Only the row past the end (position 16) was dropped; the others landed.
+    assert torch.all(kc[1, :, :Lmax - T + 1].float() == 0)
+    assert torch.all(kc[1, :, Lmax - T + 1:].float().abs().sum(-1) > 0)
+    assert torch.all(kc[0, :, :T].float().abs().sum(-1) > 0)
+
+
+@pytest.fixture(scope="module")
+def ref_model():
+    return SmolLM(make_state_dict(Config(), seed=0), Config())
+
+
+def test_smollm_prefill_then_decode_on_device_cache(cuda_dev, ref_model):
+    """Prefill 96 tokens, then 6 single-token steps, each teacher-forced with
+    the reference's greedy token; top-1 and logits against the reference's
+    CPU path with its torch.cat cache."""
+    from npu_b200.smollm_b200 import SmolLMB200, SmolLMConfig
+
+    model = SmolLMB200(make_state_dict(Config(), seed=0), SmolLMConfig(), cuda_dev)
+    ids = torch.randint(0, Config().vocab, (2, 96), generator=torch.Generator().manual_seed(3))
+    ref_logits, ref_cache = ref_model.forward(ids)
+    cache = model.new_cache(batch=2, max_len=512)
+    logits = model.forward(ids.to(cuda_dev), cache).float().cpu()
+    pos = 96
+    for step in range(7):
+        last, ref_last = logits[:, -1], ref_logits[:, -1]
+        assert torch.equal(last.argmax(-1), ref_last.argmax(-1)), step
+        assert (last - ref_last).abs().max().item() < 0.25, step
+        nxt = ref_last.argmax(-1, keepdim=True)
+        if step == 6:
+            break
+        ref_logits, ref_cache = ref_model.forward(nxt, cache=ref_cache, start_pos=pos)
+        logits = model.forward(nxt.to(cuda_dev), cache).float().cpu()
+        pos += 1
+    assert cache.lengths() == [pos, pos]
+    from npu_b200 import api
+    assert api.device_error() == 0

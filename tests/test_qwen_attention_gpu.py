@@ -1,0 +1,82 @@
+"""Qwen3.5/3.6 gated attention (qwen/forward.py:133-239) on the B200 path —
+fused per-head Q/K RMSNorm + partial RoPE + KV append, attention with the
+sigmoid gate fused into its output stores — against the reference's CPU
+attention restated in oracle/qwen_ref.py (seeded random weights; the GGUF
+checkpoint is not available offline)."""
+import pytest
+import torch
+
+from oracle import qwen_ref as R
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _block(cuda_dev, dtype=torch.float32):
+    from npu_b200.qwen_attention import QwenAttnConfig, QwenGatedAttentionB200
+
+    rc = R.QwenAttnConfig()
+    layer = R.make_layer(rc, seed=5, dtype=dtype)
+    cfg = QwenAttnConfig(d_model=rc.d_model, n_head=rc.n_head, n_head_kv=rc.n_head_kv, head_dim=rc.head_dim,
+                         rope_dim=rc.rope_dim, rms_eps=rc.rms_eps, rope_theta=rc.rope_theta, max_pos=4096)
+    blk = QwenGatedAttentionB200(layer.attn_norm, layer.wq, layer.wk, layer.wv, layer.wo, layer.q_norm,
+                                 layer.k_norm, cfg, cuda_dev)
+    cos, sin = R.partial_rope_tables(rc.rope_dim, 4096, rc.rope_theta, dtype)
+    return rc, layer, blk, cos, sin
+
+
+def test_qwen_prologue_norm_and_partial_rope(cuda_dev):
+    from npu_b200 import api
+
+    rc, layer, blk, cos, sin = _block(cuda_dev)
+    g = torch.Generator().manual_seed(2)
+    B, T, Hq, Hkv, D = 2, 7, rc.n_head, rc.n_head_kv, rc.head_dim
+    qf = torch.randn(B, T, Hq, 2, D, generator=g)
+    k = torch.randn(B, T, Hkv, D, generator=g)
+    v = torch.randn(B, T, Hkv, D, generator=g)
+    kc = torch.zeros(B, Hkv, 64, D, dtype=torch.bfloat16, device=cuda_dev)
+    vc = torch.zeros_like(kc)
+    qd = qf.to(cuda_dev)
+    q_rot = api.rope_append(qd[:, :, :, 0], k.to(cuda_dev), v.to(cuda_dev), blk.cos, blk.sin, kc, vc,
+                            start_pos=20, q_norm=blk.q_norm, k_norm=blk.k_norm, norm_eps=rc.rms_eps,
+                            rope_dim=rc.rope_dim)
+    assert api.device_error() == 0
+    cs, sn = cos[20:20 + T], sin[20:20 + T]
+    ref_q = R.partial_rope(R.rms_norm(qf[:, :, :, 0], layer.q_norm, rc.rms_eps), cs, sn, rc.rope_dim)
+    ref_k = R.partial_rope(R.rms_norm(k, layer.k_norm, rc.rms_eps), cs, sn, rc.rope_dim)
+    assert (q_rot.float().cpu() - ref_q.transpose(1, 2)).abs().max().item() < 2e-2
+    assert (kc[:, :, 20:20 + T].float().cpu() - ref_k.transpose(1, 2)).abs().max().item() < 2e-2
+    assert torch.equal(vc[:, :, 20:20 + T].cpu(), v.transpose(1, 2).to(torch.bfloat16))
+    # lanes past rope_dim are only normalised
+    assert (q_rot[..., rc.rope_dim:].float().cpu()
+            - R.rms_norm(qf[:, :, :, 0], layer.q_norm, rc.rms_eps).transpose(1, 2)[..., rc.rope_dim:]).abs().max() < 2e-2
+
+
+def test_qwen_gated_attention_prefill_then_decode(cuda_dev):
+    rc, layer, blk, cos, sin = _block(cuda_dev)
+    g = torch.Generator().manual_seed(4)
+    B, T = 2, 300
+    x = torch.randn(B, T, rc.d_model, generator=g)
+    cache = blk.new_cache(batch=B, max_len=512)
+    ref, ref_cache = R.attn_forward(x, layer, rc, cos, sin, None, 0, pre_proj=True)
+    out = blk.attention(x.to(cuda_dev), cache)
+    cache.advance()
+    assert (out.cpu() - ref).abs().max().item() <= TOL
+    pos = T
+    for step in range(3):
+        xs = torch.randn(B, 1, rc.d_model, generator=g)
+        ref, ref_cache = R.attn_forward(xs, layer, rc, cos, sin, ref_cache, pos, pre_proj=True)
+        out = blk.attention(xs.to(cuda_dev), cache)
+        cache.advance()
+        assert (out.cpu() - ref).abs().max().item() <= TOL, step
+        pos += 1
+    # One more step through the whole block (output projection included).
+    xs = torch.randn(B, 1, rc.d_model, generator=g)
+    ref_full, ref_cache = R.attn_forward(xs, layer, rc, cos, sin, ref_cache, pos)
+    full = blk.forward(xs.to(cuda_dev), cache)
+    cache.advance()
+    pos += 1
+    assert (full.cpu() - ref_full).abs().max().item() <= TOL * max(1.0, ref_full.abs().max().item())
+    assert cache.lengths() == [pos, pos]
+    from npu_b200 import api
+    assert api.device_error() == 0
