@@ -10,7 +10,9 @@ kernels read it directly with per-sequence positions, GQA heads unexpanded.
 Positions live on the device in two int32 vectors, so a step needs no host
 synchronisation: every layer's append reads the step's start positions from
 one and writes start + T into the other (the same value from each layer), the
-attention reads lengths from the second, and `advance` swaps them.
+attention reads lengths from the second, and `advance` copies the second into
+the first on the device. The buffers never move, so a step can be captured in
+a CUDA graph and replayed.
 """
 from __future__ import annotations
 
@@ -28,36 +30,36 @@ class KVCache:
         self.k = torch.zeros(shape, dtype=torch.bfloat16, device=device)
         self.v = torch.zeros(shape, dtype=torch.bfloat16, device=device)
         self._pos = torch.zeros((2, batch), dtype=torch.int32, device=device)
-        self._cur = 0
         self.max_len = max_len
         self.batch = batch
 
     @property
     def start(self) -> torch.Tensor:
         """int32 [B]: position of each sequence's next token (device)."""
-        return self._pos[self._cur]
+        return self._pos[0]
 
     @property
     def end(self) -> torch.Tensor:
         """int32 [B]: positions after the step in progress (what the appends
         write and the attention reads as sequence lengths)."""
-        return self._pos[1 - self._cur]
+        return self._pos[1]
 
     def layer(self, i: int):
         return self.k[i], self.v[i]
 
     def advance(self) -> None:
-        """Finish a step: the lengths written by this step become the next start."""
-        self._cur = 1 - self._cur
+        """Finish a step: the lengths written by this step become the next
+        start (a device copy on the current stream)."""
+        self._pos[0].copy_(self._pos[1])
 
     def reset(self, lengths=None) -> None:
         """Empty the cache (or set per-sequence lengths, e.g. after a prefill
         computed elsewhere); the stored K/V rows are left as they are."""
-        self._cur = 0
         if lengths is None:
             self._pos.zero_()
         else:
             self._pos[0].copy_(torch.as_tensor(lengths, dtype=torch.int32))
+            self._pos[1].copy_(self._pos[0])
 
     def lengths(self) -> list:
         """Host copy of the current lengths (synchronises)."""

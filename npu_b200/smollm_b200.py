@@ -124,6 +124,40 @@ class SmolLMB200:
         return o.transpose(1, 2).reshape(B, T, Hq * Dh)
 
     @torch.no_grad()
+    def capture_decode(self, cache: KVCache, warmup: int = 2):
+        """A CUDA graph of one single-token step over `cache` (every layer's
+        norm, projections, rope_append, decode attention and MLP: ~12
+        launches per layer replayed as one). Returns step(ids [B, 1]) ->
+        logits [B, 1, vocab] (a buffer the next replay overwrites). Warm-up and
+        capture run real steps; the cache's positions are restored afterwards,
+        so the rows they wrote (at most warmup + 1 past each sequence's
+        length, which must fit in max_len) are overwritten by the next tokens
+        and never read.
+        """
+        B = cache.batch
+        ids_buf = torch.zeros((B, 1), dtype=torch.long, device=self.device)
+        self._workspace(B, cache.max_len)  # allocate outside the capture
+        saved = cache._pos.clone()
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.forward(ids_buf, cache)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = self.forward(ids_buf, cache)
+        cache._pos.copy_(saved)
+
+        def step(ids: torch.Tensor) -> torch.Tensor:
+            ids_buf.copy_(ids)
+            graph.replay()
+            return out
+
+        step.graph = graph
+        return step
+
+    @torch.no_grad()
     def forward(self, ids: torch.Tensor, cache: KVCache) -> torch.Tensor:
         """Logits [B, T, vocab] for tokens ids [B, T] placed after each
         sequence's cached prefix; appends them to the cache."""

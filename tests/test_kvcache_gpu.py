@@ -96,3 +96,26 @@ def test_smollm_prefill_then_decode_on_device_cache(cuda_dev, ref_model):
     assert cache.lengths() == [pos, pos]
     from npu_b200 import api
     assert api.device_error() == 0
+
+
+def test_smollm_decode_step_as_cuda_graph(cuda_dev):
+    """A whole single-token step (30 layers, ~360 launches) captured once and
+    replayed: same logits as the eager step on an identical cache."""
+    from npu_b200 import api
+    from npu_b200.smollm_b200 import SmolLMB200, SmolLMConfig
+
+    model = SmolLMB200(make_state_dict(Config(), seed=0), SmolLMConfig(), cuda_dev)
+    ids = torch.randint(0, Config().vocab, (2, 40), generator=torch.Generator().manual_seed(9)).to(cuda_dev)
+    eager_cache, graph_cache = model.new_cache(2, 128), model.new_cache(2, 128)
+    model.forward(ids, eager_cache)
+    model.forward(ids, graph_cache)
+    step = model.capture_decode(graph_cache)
+    assert graph_cache.lengths() == [40, 40]
+    tok = ids[:, -1:]
+    for _ in range(5):
+        ref = model.forward(tok, eager_cache)
+        got = step(tok)
+        assert torch.allclose(got, ref, atol=1e-4, rtol=0)
+        tok = ref[:, -1].argmax(-1, keepdim=True)
+    assert graph_cache.lengths() == eager_cache.lengths() == [45, 45]
+    assert api.device_error() == 0
