@@ -215,8 +215,9 @@ int prefill_impl(const void* q, const void* k, const void* v, void* o, float* ls
       !strides_ok(os, 3, out_fp32 ? 4 : 8))
     return B2A_ERR_ALIGNMENT;
   if (gate && (!gs || !aligned16(gate) || !strides_ok(gs, 3, gate_bf16 ? 8 : 4))) return B2A_ERR_ALIGNMENT;
-  // Query rows per CTA: 256 (two 128-row tiles) for D <= 128, 128 for D = 256.
-  const int rows_per_cta = D == 256 ? 128 : 256;
+  // Query rows per CTA: 128 for D = 256; for D <= 128 two 128-row tiles, or
+  // one for short sequences (prefill_rows_per_cta).
+  const int rows_per_cta = D == 256 ? 128 : b2a::prefill_rows_per_cta(D, Tq, Tk);
   const long long n_qblk = (Tq + rows_per_cta - 1) / rows_per_cta;
   if (n_qblk * Hq * (long long)B > 0x7fffffffLL) return B2A_ERR_INVALID_ARG;
 
@@ -258,7 +259,7 @@ int prefill_impl(const void* q, const void* k, const void* v, void* o, float* ls
     p.gate_bf16 = gate_bf16 ? 1 : 0;
   }
   rc = D == 256 ? b2a::launch_prefill_d256(tq, tk, tv, p, static_cast<cudaStream_t>(stream))
-               : b2a::launch_prefill(D, tq, tk, tv, p, static_cast<cudaStream_t>(stream));
+               : b2a::launch_prefill(D, rows_per_cta, tq, tk, tv, p, static_cast<cudaStream_t>(stream));
   if (rc == -3) return B2A_ERR_HEAD_DIM;
   return rc ? B2A_ERR_LAUNCH : B2A_OK;
 }

@@ -6,12 +6,18 @@
 
 namespace b2a {
 
+#ifndef B2A_ONE_TILE_MAX_ROWS
+#define B2A_ONE_TILE_MAX_ROWS 512
+#endif
+// Longest query length served by one-tile CTAs (prefill_rows_per_cta).
+constexpr int kOneTileMaxRows = B2A_ONE_TILE_MAX_ROWS;
 
-template <int D>
-__global__ void __launch_bounds__(384, 1)
+
+template <int D, int NQT>
+__global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT>::CTAS_PER_SM)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ PrefillParams p) {
-  using C = PrefillCfg<D>;
+  using C = PrefillCfg<D, NQT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
@@ -33,14 +39,14 @@ __global__ void __launch_bounds__(384, 1)
   const int h = rem % p.Hq;
   const int b = rem / p.Hq;
   const int hk = h / (p.Hq / p.Hkv);
-  const int q0 = qblk * 256;
+  const int q0 = qblk * (C::BM * C::NQT);
   const int sp = p.start_pos_arr ? p.start_pos_arr[b] : p.start_pos;
   // Key blocks each query tile needs: n_t[t] for tile t; tile 0 (earlier rows)
   // never needs more blocks than tile 1, and under the causal mask at most one
   // fewer. n_kv = n_t[1] is what gets loaded.
-  int n_t[2];
+  int n_t[C::NQT];
 #pragma unroll
-  for (int t = 0; t < 2; ++t) {
+  for (int t = 0; t < C::NQT; ++t) {
     if (p.causal) {
       const int last_row = min(q0 + (t + 1) * C::BM - 1, p.Tq - 1);
       const long long kv_end = min((long long)p.Tk, (long long)sp + last_row + 1);
@@ -49,7 +55,7 @@ __global__ void __launch_bounds__(384, 1)
       n_t[t] = (p.Tk + C::BN - 1) / C::BN;
     }
   }
-  const int n_kv = n_t[1];
+  const int n_kv = n_t[C::NQT - 1];
   const int n0 = n_t[0];
 
   if (threadIdx.x == 0) {
@@ -57,10 +63,10 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&bars->kv_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 2);  // released by both UMMA issuers
+      mbar_init(&bars->kv_empty[s], C::NQT);  // released by every UMMA issuer
     }
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < C::NQT; ++t) {
       mbar_init(&bars->sa_full[t], 1);
       mbar_init(&bars->sb_full[t], 1);
       mbar_init(&bars->mid[t], 4);       // one arrive per softmax warp
@@ -68,8 +74,8 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&bars->pva_done[t], 1);
       mbar_init(&bars->o_full[t], 1);
     }
-    mbar_init(&bars->drain[0], 1);
-    mbar_init(&bars->drain[1], 1);
+#pragma unroll
+    for (int t = 0; t < C::NQT; ++t) mbar_init(&bars->drain[t], 1);
     bars->abort_flag = 0;
     fence_mbar_init();
   }
@@ -123,10 +129,10 @@ __global__ void __launch_bounds__(384, 1)
       for (int i = max(0, issued - C::STAGES); i < issued; ++i)
         mbar_wait_quiet(&bars->kv_full[i % C::STAGES], (uint32_t)(i / C::STAGES) & 1u);
     }
-  } else if (n_kv > 0 && (warp == 1 || warp == 2)) {
+  } else if (n_kv > 0 && warp >= 1 && warp <= C::NQT) {
     // ------------------------------------------------------------ UMMA issuers
-    // Warp 1 issues tile 0's MMAs, warp 2 tile 1's. Both read every K/V
-    // tile they need and release it (kv_empty counts two arrivals).
+    // Warp 1 issues tile 0's MMAs, warp 2 (NQT = 2) tile 1's. Each reads
+    // every K/V tile it needs and releases it (kv_empty counts NQT arrivals).
     const int t = warp - 1;
     const int nt = t == 0 ? n0 : n_kv;
     constexpr uint32_t IDESC_S = umma_idesc_bf16(128, C::HALF, false);
@@ -361,28 +367,38 @@ __global__ void __launch_bounds__(384, 1)
 }
 
 // ------------------------------------------------------------------ launcher
-template <int D>
+template <int D, int NQT>
 static int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                             const PrefillParams& p, cudaStream_t st) {
-  using C = PrefillCfg<D>;
-  cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  using C = PrefillCfg<D, NQT>;
+  cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<D, NQT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM_BYTES);
   if (e != cudaSuccess) return -1;
   // The in-kernel register split needs at least MIN_LAUNCH_REGS per thread.
   cudaFuncAttributes fa{};
-  if (cudaFuncGetAttributes(&fa, fa_prefill_kernel<D>) != cudaSuccess || fa.numRegs < C::MIN_LAUNCH_REGS)
+  if (cudaFuncGetAttributes(&fa, fa_prefill_kernel<D, NQT>) != cudaSuccess || fa.numRegs < C::MIN_LAUNCH_REGS)
     return -1;
   const long long nblk = (long long)p.n_qblk * p.Hq * p.B;
   if (nblk <= 0 || nblk > 0x7fffffffLL) return -2;
-  fa_prefill_kernel<D><<<(unsigned)nblk, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, p);
+  fa_prefill_kernel<D, NQT><<<(unsigned)nblk, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-int launch_prefill(int D, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+// One-tile CTAs (two per SM) pay off when a CTA sees few key blocks, so that
+// its start-up and epilogue are a large share of its time.
+int prefill_rows_per_cta(int D, int Tq, int Tk) {
+  (void)D;
+  (void)Tk;
+  return Tq <= kOneTileMaxRows ? 128 : 256;
+}
+
+int launch_prefill(int D, int rows_per_cta, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                    const PrefillParams& p, cudaStream_t st) {
+  const bool one = rows_per_cta == 128;
   switch (D) {
-    case 64: return launch_prefill_t<64>(tq, tk, tv, p, st);
-    case 128: return launch_prefill_t<128>(tq, tk, tv, p, st);
+    case 64: return one ? launch_prefill_t<64, 1>(tq, tk, tv, p, st) : launch_prefill_t<64, 2>(tq, tk, tv, p, st);
+    case 128:
+      return one ? launch_prefill_t<128, 1>(tq, tk, tv, p, st) : launch_prefill_t<128, 2>(tq, tk, tv, p, st);
     default: return -3;
   }
 }

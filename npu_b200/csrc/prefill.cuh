@@ -52,7 +52,7 @@ struct PrefillParams {
   float scale_log2;    // softmax scale * log2(e)
   int causal;
   int out_fp32;
-  int n_qblk;          // ceil(Tq / 256)
+  int n_qblk;          // ceil(Tq / (128 * query tiles per CTA))
   int* err;            // device error word (may be nullptr)
   // Optional output gate [B, Hq, Tq, D] (element strides g_sb, g_sh, g_st,
   // innermost 1; fp32 or bf16): o = attention * sigmoid(gate), the gated
@@ -62,36 +62,45 @@ struct PrefillParams {
   int gate_bf16;
 };
 
-template <int D>
+// NQT query tiles of 128 rows per CTA. NQT = 2: the two tiles' softmax and
+// MMAs interleave inside one CTA (one CTA per SM). NQT = 1: half the shared
+// memory and TMEM, so two CTAs share an SM and one's start-up and epilogue
+// overlap the other's steady state — the better choice when each CTA sees
+// few key blocks (short sequences).
+template <int D, int NQT_ = 2>
 struct PrefillCfg {
   static constexpr int BM = 128;  // rows per Q tile == TMEM lanes
   static constexpr int BN = 128;  // keys per K/V tile
-  static constexpr int NQT = 2;   // Q tiles per CTA
+  static constexpr int NQT = NQT_;  // Q tiles per CTA
   static constexpr int KCH = D / 64;  // 128-byte swizzle chunks per row
   static constexpr int CHUNK_BYTES = 128 * 128;  // 128 rows x 128 B
   static constexpr int Q_TILE_BYTES = BM * D * 2;
   static constexpr int KV_TILE_BYTES = BN * D * 2;
-  static constexpr int STAGES = (D == 64) ? 8 : 5;
+  static constexpr int STAGES = NQT == 2 ? ((D == 64) ? 8 : 5) : ((D == 64) ? 4 : 2);
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = OFF_Q + NQT * Q_TILE_BYTES;
   static constexpr int OFF_BAR = OFF_KV + STAGES * KV_TILE_BYTES;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
-  static constexpr int TMEM_COLS = 512;
+  static constexpr int CTAS_PER_SM = NQT == 2 ? 1 : 2;
+  static constexpr int TMEM_COLS = NQT == 2 ? 512 : 256;
   static constexpr int S_COL = 0;          // S/P region R_t at S_COL + t * BN
   static constexpr int HALF = BN / 2;      // keys per S half (one N = 64 UMMA group)
   static constexpr int O_COL = NQT * BN;   // O_t at O_COL + t * D
-  static constexpr int THREADS = 384;
+  static constexpr int THREADS = 128 + 128 * NQT;
   // setmaxnreg split: warpgroup 0 (TMA + MMA issue) gives registers to the
-  // two softmax warpgroups. 128 * REGS_LOW + 256 * REGS_HIGH = 61440 = 384 * 160,
-  // so any launch with >= MIN_LAUNCH_REGS registers per thread covers it (the
-  // launcher refuses to launch otherwise).
-  static constexpr int REGS_LOW = 112;
-  static constexpr int REGS_HIGH = 184;
-  static constexpr int MIN_LAUNCH_REGS = (128 * REGS_LOW + 256 * REGS_HIGH + THREADS - 1) / THREADS;
+  // softmax warpgroups. The sum 128 * REGS_LOW + 128 * NQT * REGS_HIGH stays
+  // within THREADS * MIN_LAUNCH_REGS, so any launch with >= MIN_LAUNCH_REGS
+  // registers per thread covers it (the launcher refuses to launch otherwise;
+  // 168 for NQT = 2, 128 for NQT = 1 at two CTAs per SM).
+  static constexpr int REGS_LOW = NQT == 2 ? 112 : 88;
+  static constexpr int REGS_HIGH = NQT == 2 ? 184 : 168;
+  static constexpr int MIN_LAUNCH_REGS = (128 * REGS_LOW + 128 * NQT * REGS_HIGH + THREADS - 1) / THREADS;
   static_assert(D == 64 || D == 128, "two-tile prefill supports head_dim 64 and 128");
+  static_assert(NQT == 1 || NQT == 2, "one or two query tiles per CTA");
   static_assert(O_COL + NQT * D <= TMEM_COLS, "TMEM budget");
-  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(SMEM_BYTES * CTAS_PER_SM <= 232448 - 1024 * (CTAS_PER_SM - 1), "shared memory budget");
+  static_assert(MIN_LAUNCH_REGS * THREADS * CTAS_PER_SM <= 65536, "register budget");
 };
 
 // Barrier slots inside the OFF_BAR region.
@@ -115,9 +124,14 @@ struct PrefillBars {
 int launch_prefill_d256(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                         const PrefillParams& p, cudaStream_t st);
 
-// Launch the prefill kernel on `st`. Returns 0 on success, -3 for an
-// unsupported head_dim, another negative value on launch failure.
-int launch_prefill(int D, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+// Query rows per CTA the D <= 128 kernel will use for this problem (256 or
+// 128; PrefillParams::n_qblk must be computed with it).
+int prefill_rows_per_cta(int D, int Tq, int Tk);
+
+// Launch the prefill kernel on `st` with rows_per_cta query rows per CTA.
+// Returns 0 on success, -3 for an unsupported head_dim, another negative
+// value on launch failure.
+int launch_prefill(int D, int rows_per_cta, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                    const PrefillParams& p, cudaStream_t st);
 
 }  // namespace b2a
