@@ -16,7 +16,8 @@ constexpr int kOneTileMaxRows = B2A_ONE_TILE_MAX_ROWS;
 template <int D, int NQT>
 __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT>::CTAS_PER_SM)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ PrefillParams p) {
+                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                      const __grid_constant__ PrefillParams p) {
   using C = PrefillCfg<D, NQT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
@@ -337,8 +338,12 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
         for (int c = 0; c < D / 32; ++c) store_out_chunk(p, b, h, grow, c, z, 0.f);
         if (p.lse) p.lse[((long long)b * p.Hq + h) * p.Tq + grow] = -INFINITY;
       }
-    } else if (ok) {
-      const bool w = mbar_wait(&bars->o_full[t], 0, abort_flag, p.err);
+    } else {
+      const bool w = ok && mbar_wait(&bars->o_full[t], 0, abort_flag, p.err);
+      // With o_tma the tile's rows are staged in its Q buffer, which no MMA
+      // reads any more (all of tile t's S MMAs completed before o_full[t]),
+      // and written out by one TMA store; rows past Tq are clipped by it.
+      const uint32_t stage = smem_u32(sQ + t * C::Q_TILE_BYTES);
       if (__all_sync(0xffffffffu, w)) {
         tc_fence_after();
         const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
@@ -347,11 +352,35 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
           uint32_t o[32];
           tmem_ld32(tO + 32 * c, o);
           tmem_wait_ld();
-          if (valid) store_out_chunk(p, b, h, grow, c, o, inv_l);
+          if (p.o_tma) {
+            float v[32];
+            if (valid) {
+              out_chunk_values(p, b, h, grow, c, o, inv_l, v);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = 0.f;
+            }
+            stage_out_chunk_bf16(stage, C::CHUNK_BYTES, row, c, v);
+          } else if (valid) {
+            store_out_chunk(p, b, h, grow, c, o, inv_l);
+          }
         }
         if (p.lse && valid) {
           p.lse[((long long)b * p.Hq + h) * p.Tq + grow] =
               l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994531f : -INFINITY;
+        }
+      }
+      if (p.o_tma) {
+        // Every thread of the tile's warpgroup arrives here exactly once
+        // (this branch is tile-uniform), also on the abort path.
+        fence_proxy_async_smem();
+        named_bar_sync(1 + t, 128);
+        if (row == 0 && !*abort_flag) {
+#pragma unroll
+          for (int c = 0; c < C::KCH; ++c)
+            tma_store_4d(&tm_o, sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, c * 64, q0 + t * C::BM, h, b);
+          tma_store_commit();
+          tma_store_wait_read();  // the staging buffer must outlive the copy's reads
         }
       }
     }
@@ -369,7 +398,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
 // ------------------------------------------------------------------ launcher
 template <int D, int NQT>
 static int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                            const PrefillParams& p, cudaStream_t st) {
+                            const CUtensorMap& to, const PrefillParams& p, cudaStream_t st) {
   using C = PrefillCfg<D, NQT>;
   cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<D, NQT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM_BYTES);
@@ -380,7 +409,7 @@ static int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const 
     return -1;
   const long long nblk = (long long)p.n_qblk * p.Hq * p.B;
   if (nblk <= 0 || nblk > 0x7fffffffLL) return -2;
-  fa_prefill_kernel<D, NQT><<<(unsigned)nblk, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, p);
+  fa_prefill_kernel<D, NQT><<<(unsigned)nblk, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, to, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -393,12 +422,14 @@ int prefill_rows_per_cta(int D, int Tq, int Tk) {
 }
 
 int launch_prefill(int D, int rows_per_cta, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                   const PrefillParams& p, cudaStream_t st) {
+                   const CUtensorMap& to, const PrefillParams& p, cudaStream_t st) {
   const bool one = rows_per_cta == 128;
   switch (D) {
-    case 64: return one ? launch_prefill_t<64, 1>(tq, tk, tv, p, st) : launch_prefill_t<64, 2>(tq, tk, tv, p, st);
+    case 64:
+      return one ? launch_prefill_t<64, 1>(tq, tk, tv, to, p, st) : launch_prefill_t<64, 2>(tq, tk, tv, to, p, st);
     case 128:
-      return one ? launch_prefill_t<128, 1>(tq, tk, tv, p, st) : launch_prefill_t<128, 2>(tq, tk, tv, p, st);
+      return one ? launch_prefill_t<128, 1>(tq, tk, tv, to, p, st)
+                 : launch_prefill_t<128, 2>(tq, tk, tv, to, p, st);
     default: return -3;
   }
 }

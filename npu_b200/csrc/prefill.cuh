@@ -60,6 +60,10 @@ struct PrefillParams {
   const void* gate;
   long long g_sb, g_sh, g_st;
   int gate_bf16;
+  // 1: O is bf16 and the kernel's O tensor map is valid, so each tile's
+  // output goes through shared memory (the tile's spent Q buffer) and one
+  // TMA store instead of per-row global stores.
+  int o_tma;
 };
 
 // NQT query tiles of 128 rows per CTA. NQT = 2: the two tiles' softmax and
@@ -131,7 +135,9 @@ int prefill_rows_per_cta(int D, int Tq, int Tk);
 // Launch the prefill kernel on `st` with rows_per_cta query rows per CTA.
 // Returns 0 on success, -3 for an unsupported head_dim, another negative
 // value on launch failure.
+// `to` describes O (4-D, 64-column x 128-row boxes, 128-byte swizzle) when
+// p.o_tma is set; it is not read otherwise.
 int launch_prefill(int D, int rows_per_cta, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                   const PrefillParams& p, cudaStream_t st);
+                   const CUtensorMap& to, const PrefillParams& p, cudaStream_t st);
 
 }  // namespace b2a

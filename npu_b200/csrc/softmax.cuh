@@ -264,11 +264,10 @@ __device__ __forceinline__ float softmax_half_tmem(uint32_t (&s)[2][32], int lim
 // sigmoid(g) = 1 / (1 + e^-g) in fp32 (torch.sigmoid, qwen/forward.py:226).
 __device__ __forceinline__ float sigmoidf_(float g) { return __fdividef(1.f, 1.f + __expf(-g)); }
 
-// Scale one 32-column chunk of an output row by inv_l (and, with a gate, by
-// sigmoid(gate)) and store it (fp32 or bf16) with 16-byte stores.
-__device__ __forceinline__ void store_out_chunk(const PrefillParams& p, int b, int h, int grow, int c,
-                                                const uint32_t (&o)[32], float inv_l) {
-  float v[32];
+// One 32-column chunk of an output row: O scaled by inv_l and, with a gate,
+// by sigmoid(gate). Only called for rows that exist (the gate is read).
+__device__ __forceinline__ void out_chunk_values(const PrefillParams& p, int b, int h, int grow, int c,
+                                                 const uint32_t (&o)[32], float inv_l, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = u2f(o[i]) * inv_l;
   if (p.gate) {
@@ -297,6 +296,14 @@ __device__ __forceinline__ void store_out_chunk(const PrefillParams& p, int b, i
       }
     }
   }
+}
+
+// Scale one 32-column chunk of an output row (out_chunk_values) and store it
+// (fp32 or bf16) with 16-byte stores.
+__device__ __forceinline__ void store_out_chunk(const PrefillParams& p, int b, int h, int grow, int c,
+                                                const uint32_t (&o)[32], float inv_l) {
+  float v[32];
+  out_chunk_values(p, b, h, grow, c, o, inv_l, v);
   const long long base = (long long)b * p.o_sb + (long long)h * p.o_sh + (long long)grow * p.o_st + 32 * c;
   if (p.out_fp32) {
     float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.o) + base);
@@ -313,6 +320,22 @@ __device__ __forceinline__ void store_out_chunk(const PrefillParams& p, int b, i
       w.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
       dst[i] = w;
     }
+  }
+}
+
+// Write one 32-column chunk (bf16) of an output row into a 128-row tile in
+// shared memory laid out as a TMA SWIZZLE_128B box of 64 columns: chunk c of
+// row r goes to 64-column block c / 2, 16-byte units (c % 2) * 4 .. + 3, each
+// unit index XORed with (r & 7). The tile is then stored with tma_store_4d.
+__device__ __forceinline__ void stage_out_chunk_bf16(uint32_t tile, int block_bytes, int r, int c,
+                                                     const float (&v)[32]) {
+  const uint32_t base = tile + (c >> 1) * block_bytes + r * 128;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int unit = (c & 1) * 4 + u;
+    st_shared_v4(base + ((unit ^ (r & 7)) << 4), pack_bf16x2(v[8 * u], v[8 * u + 1]),
+                 pack_bf16x2(v[8 * u + 2], v[8 * u + 3]), pack_bf16x2(v[8 * u + 4], v[8 * u + 5]),
+                 pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
   }
 }
 

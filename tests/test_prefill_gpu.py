@@ -124,6 +124,24 @@ def test_strided_bthd_inputs(cuda_dev):
     assert (out.cpu() - ref).abs().max().item() <= TOL
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_bf16_output_into_strided_bthd_buffer(cuda_dev, D):
+    """bf16 output written into a [B, T, H, D] buffer viewed as [B, H, T, D]
+    (the layout the output projection reads), with a ragged T: the tile store
+    must clip the rows past T and leave the rest of the buffer untouched."""
+    from npu_b200 import api
+
+    g = torch.Generator().manual_seed(15 + D)
+    B, T, Hq, Hkv = 2, 300, 8, 2
+    q, k, v = _rand((B, Hq, T, D), g, cuda_dev), _rand((B, Hkv, T, D), g, cuda_dev), _rand((B, Hkv, T, D), g, cuda_dev)
+    buf = torch.full((B, T + 5, Hq, D), 7.0, dtype=torch.bfloat16, device=cuda_dev)
+    out = buf[:, :T].transpose(1, 2)
+    api.prefill(q, k, v, out_dtype=torch.bfloat16, out=out)
+    ref = A.dense_attention(q.cpu(), k.cpu(), v.cpu())
+    assert (out.float().cpu() - ref).abs().max().item() <= TOL
+    assert torch.all(buf[:, T:] == 7.0)
+
+
 def test_fully_masked_rows_and_empty_keys(cuda_dev):
     from npu_b200 import api
 
