@@ -22,6 +22,15 @@ extern "C" {
  */
 B2A_API int b2a_diag_umma_gemm(const void* a, const void* b, float* c, int b_mn_major, void* stream);
 
+/*
+ * Launch one CTA that waits on an mbarrier nothing arrives on, with the same
+ * bounded wait the kernels use but a limit of `limit_cycles` (1 .. 4e9). The
+ * wait runs out, sets the abort path and the device error word, and the
+ * kernel exits; b2a_get_device_error then reports B2A_ERR_DEVICE_TIMEOUT.
+ * Used by the GPU tests to check failure reporting without a GPU fault.
+ */
+B2A_API int b2a_diag_wait_timeout(long long limit_cycles, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -92,6 +92,7 @@ SIGNATURES = {
     # include/b2attn_diag.h
     "b2a_diag_umma_gemm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                           ctypes.c_void_p]),
+    "b2a_diag_wait_timeout": (ctypes.c_int, [ctypes.c_longlong, ctypes.c_void_p]),
 }
 
 

@@ -333,6 +333,13 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
 
 }  // namespace
 
+namespace b2a {
+int* device_error_word() {
+  const int dev = current_device();
+  return dev < 0 ? nullptr : device_err_ptr(dev);
+}
+}  // namespace b2a
+
 extern "C" {
 
 const char* b2a_strerror(int code) {

@@ -25,6 +25,10 @@ enum : int {
   kErrBadArgs = 2,
 };
 
+// Device address of the error word on the current device (set up by the C
+// ABI layer; nullptr if it cannot be obtained).
+int* device_error_word();
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -61,20 +65,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Wait until the phase with the given parity has completed. Returns false if
 // the CTA is aborting (another role timed out) or if this wait itself ran past
-// the cycle bound, in which case it raises the abort flag and the error word.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* err) {
+// `limit` cycles, in which case it raises the abort flag and the error word.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                                long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       if (err) atomicOr(err, kErrWaitTimeout);
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* err) {
+  return mbar_wait_limit(bar, parity, abort_flag, err, kWaitLimitCycles);
 }
 
 // Bounded wait that ignores the abort flag: used on the abort path to let

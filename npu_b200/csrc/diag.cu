@@ -99,7 +99,31 @@ __global__ void __launch_bounds__(128) diag_umma_kernel(const __nv_bfloat16* A, 
   }
 }
 
+// A wait on an mbarrier that nothing ever arrives on, bounded by `limit`
+// cycles: the failure path every kernel's waits take (abort flag, error word,
+// orderly exit) exercised on purpose, without faulting or hanging the GPU.
+__global__ void __launch_bounds__(32) diag_wait_timeout_kernel(long long limit, int* err) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncwarp();
+  const bool ok = mbar_wait_limit(&bar, 0, &abort_flag, threadIdx.x == 0 ? err : nullptr, limit);
+  (void)ok;
+}
+
 }  // namespace b2a
+
+extern "C" int b2a_diag_wait_timeout(long long limit_cycles, void* stream) {
+  if (limit_cycles <= 0 || limit_cycles > 4000000000LL) return -1;
+  int* err = b2a::device_error_word();
+  if (!err) return -11;
+  b2a::diag_wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_cycles, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -6;
+}
 
 extern "C" int b2a_diag_umma_gemm(const void* a, const void* b, float* c, int b_mn_major, void* stream) {
   if (!a || !b || !c) return -1;

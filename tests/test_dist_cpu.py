@@ -92,3 +92,49 @@ def test_context_parallel_prefill_gloo(world):
         assert p.exitcode == 0
     assert len(result) == world
     assert max(result.values()) < 1e-5
+
+
+def _dead_peer_worker(rank, world, port, result):
+    """Rank 1 joins the group and exits without reaching the collective;
+    rank 0's K/V all-gather must fail within the group's timeout, not hang."""
+    import datetime
+    import os
+    import time
+
+    import torch.distributed as dist
+
+    from npu_b200.dist import ContextParallelPrefill
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(0)  # dies between steps, with nothing in flight
+    cp = ContextParallelPrefill(256, world, rank)
+    k = torch.zeros(1, 1, 2 * cp.c, 64)
+    t0 = time.time()
+    try:
+        cp.gather_kv(k, k)
+        result[rank] = ("no error", time.time() - t0)
+    except Exception as e:  # gloo reports the lost peer (closed connection or timeout)
+        result[rank] = (type(e).__name__, time.time() - t0)
+
+
+def test_dead_peer_is_detected_on_the_host():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    result = mgr.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_dead_peer_worker, args=(r, 2, port, result)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert 0 in result, "rank 0 neither finished nor failed"
+    err, secs = result[0]
+    assert err != "no error"
+    assert secs < 60
