@@ -10,9 +10,10 @@
  * re-entrant and ordered on the caller's CUDA stream.
  *
  * Conventions
- *  - All tensor pointers are caller-owned device memory; nothing here
- *    allocates on the call path. Decode scratch comes from the caller
- *    (b2a_decode_workspace_bytes).
+ *  - All tensor pointers are caller-owned device memory (b2a_prefill_host:
+ *    host memory, plus a device workspace); nothing here allocates on the
+ *    call path. Scratch comes from the caller (b2a_decode_workspace_bytes,
+ *    b2a_prefill_host_workspace_bytes).
  *  - Element types: Q/K/V and the KV cache are bf16. Outputs are bf16 or fp32
  *    (out_fp32). Innermost (head_dim) stride is 1; every other stride is given
  *    in ELEMENTS and must be a multiple of 8 (16 bytes). Base pointers must be
@@ -222,6 +223,39 @@ B2A_API int b2a_qk_norm_rope_append(const void* q, const void* k, const void* v,
                                     const long long* v_cache_strides, int B, int T, int Hq, int Hkv, int D,
                                     int Lmax, int start_pos, const int* start_pos_per_batch, int* seqlens_out,
                                     void* stream);
+
+/*
+ * Prefill with inputs and result in HOST memory: the call surface of the
+ * reference's NpuAttention.run_batch (npu/fa.py:206-323), which takes host
+ * Q/K/V stacks and returns the host O stack.
+ *
+ *   q   [B, Hq,  Tq, D]  bf16, contiguous, host memory
+ *   k   [B, Hkv, Tk, D]  bf16, contiguous, host memory (may be NULL if Tk == 0)
+ *   v   [B, Hkv, Tk, D]
+ *   o   [B, Hq,  Tq, D]  bf16 (fp32 if out_fp32), contiguous, host memory
+ *   start_pos_per_batch  optional HOST int32 [B]; else start_pos for all
+ *   workspace  device memory of b2a_prefill_host_workspace_bytes(...) bytes,
+ *              256-byte aligned
+ *
+ * Same arithmetic, masking and results as b2a_prefill. The problem is cut
+ * into n_chunks pieces of (batch, KV head) units (0 = 32): whole batches
+ * when there are enough, else KV heads of one batch. Each piece is copied in
+ * on a library-owned copy stream, computed on `stream`, and copied out on a
+ * second copy stream, with two workspace slots alternating, so uploads,
+ * kernels and downloads of neighbouring pieces overlap. The call is
+ * asynchronous and ordered on `stream`: it returns once everything is
+ * queued, and work queued on `stream` afterwards (a synchronize, an event)
+ * sees the complete o. Host buffers must stay valid and unmodified until
+ * then. Page-locked host memory is needed for the copies to overlap;
+ * pageable buffers give the same result with the copies serialised.
+ * Concurrent calls on one device are serialised while queueing and must not
+ * share a workspace unless ordered on one stream.
+ */
+B2A_API size_t b2a_prefill_host_workspace_bytes(int B, int Hq, int Hkv, int Tq, int Tk, int D, int out_fp32,
+                                                int n_chunks);
+B2A_API int b2a_prefill_host(const void* q, const void* k, const void* v, void* o, int B, int Hq, int Hkv, int Tq,
+                             int Tk, int D, int start_pos, const int* start_pos_per_batch, float scale, int causal,
+                             int out_fp32, int n_chunks, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Read (and optionally clear) the device error word the kernels set on the

@@ -117,6 +117,89 @@ def prefill(
     return (out, lse) if return_lse else out
 
 
+def prefill_host_workspace_bytes(B: int, Hq: int, Hkv: int, Tq: int, Tk: int, D: int,
+                                 out_fp32: bool = False, n_chunks: int = 0) -> int:
+    return int(_lib.load().b2a_prefill_host_workspace_bytes(B, Hq, Hkv, Tq, Tk, D, 1 if out_fp32 else 0,
+                                                            n_chunks))
+
+
+def prefill_host(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    start_pos: int = 0,
+    start_pos_per_batch=None,
+    scale: Optional[float] = None,
+    causal: bool = True,
+    out_dtype: torch.dtype = torch.bfloat16,
+    out: Optional[torch.Tensor] = None,
+    n_chunks: int = 0,
+    device: Optional[torch.device] = None,
+    workspace: Optional[torch.Tensor] = None,
+    sync: bool = True,
+) -> torch.Tensor:
+    """`prefill` for tensors in HOST memory (b2a_prefill_host): q [B, Hq, Tq, D]
+    and k/v [B, Hkv, Tk, D] contiguous bf16 CPU tensors, result o [B, Hq, Tq, D]
+    on the host (page-locked when allocated here). The work is cut into
+    n_chunks pieces whose uploads, kernels and downloads overlap on the GPU
+    `device` (default: the current one). start_pos_per_batch, if given, is a
+    host sequence / CPU int32 tensor [B]. With sync=False the call returns once
+    the copies and kernels are queued on the device's current stream; the
+    inputs must then stay untouched and `out` unread until that stream is
+    synchronised. Page-locked inputs (`tensor.pin_memory()`) are needed for the
+    copies to overlap; pageable ones give the same result, serialised.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not isinstance(t, torch.Tensor) or t.is_cuda:
+            raise ValueError(f"{name} must be a CPU tensor (use prefill for device tensors)")
+        if t.dtype != torch.bfloat16 or t.dim() != 4 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous 4-d bfloat16 tensor, got {t.dtype} {tuple(t.shape)}")
+    B, Hq, Tq, D = q.shape
+    Bk, Hkv, Tk, Dk = k.shape
+    if (Bk, Dk) != (B, D) or tuple(v.shape) != tuple(k.shape):
+        raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("out_dtype must be float32 or bfloat16")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty((B, Hq, Tq, D), dtype=out_dtype, pin_memory=True)
+    elif (out.is_cuda or out.dtype != out_dtype or tuple(out.shape) != (B, Hq, Tq, D)
+          or not out.is_contiguous()):
+        raise ValueError("out must be a contiguous CPU tensor [B, Hq, Tq, D] of out_dtype")
+    spb = None
+    if start_pos_per_batch is not None:
+        spb = torch.as_tensor(start_pos_per_batch, dtype=torch.int32).contiguous()
+        if spb.is_cuda or spb.numel() != B:
+            raise ValueError("start_pos_per_batch must be a host sequence of B int32 positions")
+    if device is None:
+        if not torch.cuda.is_available():
+            raise RuntimeError("prefill_host needs a CUDA device (no CPU path)")
+        device = torch.device("cuda", torch.cuda.current_device())
+    device = torch.device(device)
+    out_fp32 = out_dtype == torch.float32
+    lib = _lib.load()
+    need = int(lib.b2a_prefill_host_workspace_bytes(B, Hq, Hkv, Tq, Tk, D, 1 if out_fp32 else 0, n_chunks))
+    if need == 0:
+        _lib.check(_lib.B2A_ERR_INVALID_ARG, "b2a_prefill_host_workspace_bytes")
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=device)
+    elif not workspace.is_cuda or workspace.device != device or workspace.numel() < need:
+        raise ValueError(f"workspace must be a CUDA uint8 tensor of >= {need} bytes on {device}")
+    with torch.cuda.device(device):
+        rc = lib.b2a_prefill_host(
+            q.data_ptr(), k.data_ptr() if Tk else None, v.data_ptr() if Tk else None, out.data_ptr(),
+            B, Hq, Hkv, Tq, Tk, D, int(start_pos), spb.data_ptr() if spb is not None else None,
+            float(scale), 1 if causal else 0, 1 if out_fp32 else 0, int(n_chunks),
+            workspace.data_ptr(), workspace.numel(), _stream_ptr(device),
+        )
+        _lib.check(rc, "b2a_prefill_host")
+        if sync:
+            torch.cuda.current_stream(device).synchronize()
+    return out
+
+
 def decode_workspace_bytes(B: int, Hq: int, Hkv: int, D: int, Lmax: int, split_len: int = 0) -> int:
     return int(_lib.load().b2a_decode_workspace_bytes(B, Hq, Hkv, D, Lmax, split_len))
 

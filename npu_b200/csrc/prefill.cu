@@ -19,6 +19,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                       const __grid_constant__ PrefillParams p) {
   using C = PrefillCfg<D, NQT>;
+  constexpr int kEmuPairs = exp2_emu_pairs<D>();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
@@ -273,7 +274,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
       tmem_ld32(tR + fcol + 32, s[1]);
       tmem_wait_ld();
       float hs0, hs1;
-      const float a0 = softmax_half_tmem(s, lim, sl2, m_run, tR + fcol, hs0);
+      const float a0 = softmax_half_tmem<kEmuPairs>(s, lim, sl2, m_run, tR + fcol, hs0);
       auto rescale_O = [&](float f) {
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
@@ -307,7 +308,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->mid[t]);
-      const float a1 = softmax_half_tmem(s, lim - C::HALF, sl2, m_run, tR + fcol + 32, hs1);
+      const float a1 = softmax_half_tmem<kEmuPairs>(s, lim - C::HALF, sl2, m_run, tR + fcol + 32, hs1);
       if (__any_sync(0xffffffffu, a1 != 1.f)) {
         // Rare: the second half moved the running max. O then holds blocks
         // < j and the first half of block j (once its PV half completes);

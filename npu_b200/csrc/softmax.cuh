@@ -16,6 +16,15 @@ namespace b2a {
 constexpr int kExp2EmuPairs = B2A_EXP2_EMU;
 static_assert(kExp2EmuPairs >= 0 && kExp2EmuPairs <= 4, "B2A_EXP2_EMU is a count out of 4 pairs");
 
+// The split that measured fastest per head dim on B200 (causal prefill,
+// T = 1k-8k): at D = 64, where the exponentials are the largest share of a
+// block's work, one pair in four on the FMA pipe is ~5 % faster; at D = 128
+// all on MUFU is 2-4 % faster; D = 256 measures the same either way.
+template <int D>
+__host__ __device__ constexpr int exp2_emu_pairs() {
+  return D == 128 ? 0 : kExp2EmuPairs;
+}
+
 __device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
 __device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
 
@@ -163,7 +172,7 @@ __device__ __forceinline__ float softmax_p_row_tmem(const uint32_t (&s)[BN / 32]
 // are still in flight (the P columns written here, tP + 16 q, lie below the
 // S columns of any later chunk). Same pipe split and TMEM store rules as
 // softmax_p_row_tmem.
-template <int NCH, int Q0, int NQ, bool kEmu, bool kTrackMax>
+template <int NCH, int Q0, int NQ, int kEmuPairs, bool kTrackMax>
 __device__ __forceinline__ void softmax_p_chunks_tmem(const uint32_t (&s)[NCH][32], float sl2, float m_use,
                                                       uint32_t tP, float2 (&acc)[4], float (&mx)[4]) {
   const float2 sc2 = make_float2(sl2, sl2);
@@ -176,7 +185,7 @@ __device__ __forceinline__ void softmax_p_chunks_tmem(const uint32_t (&s)[NCH][3
       if (kTrackMax) mx[pp & 3] = fmax3(mx[pp & 3], u2f(s[q][2 * pp]), u2f(s[q][2 * pp + 1]));
       const float2 x = __ffma2_rn(make_float2(u2f(s[q][2 * pp]), u2f(s[q][2 * pp + 1])), sc2, nm2);
       float2 e;
-      if (kEmu && (pp & 3) < kExp2EmuPairs)
+      if ((pp & 3) < kEmuPairs)
         e = exp2_fma2(x);
       else
         e = make_float2(ex2(x.x), ex2(x.y));
@@ -202,7 +211,9 @@ constexpr float kRescaleThreshold = 8.0f;
 // take the max first. Returns the factor (<= 1) by which everything summed
 // for this row before this half (earlier blocks, the block's earlier half,
 // their P and O) has to be scaled: 1 unless m_run moved. `hsum` receives the
-// half's sum of P. Warp-collective (TMEM stores, votes): all lanes call it.
+// half's sum of P. kEmuPairs of every 4 column pairs use the FMA-pipe exp2 on
+// unmasked halves. Warp-collective (TMEM stores, votes): all lanes call it.
+template <int kEmuPairs>
 __device__ __forceinline__ float softmax_half_tmem(uint32_t (&s)[2][32], int lim, float sl2, float& m_run,
                                                    uint32_t tP, float& hsum) {
   const bool full = __all_sync(0xffffffffu, lim >= 63);
@@ -222,9 +233,9 @@ __device__ __forceinline__ float softmax_half_tmem(uint32_t (&s)[2][32], int lim
   if (__all_sync(0xffffffffu, m_run != -INFINITY)) {
     // exp2 on both pipes only when no key is masked (no -inf inputs).
     if (full)
-      softmax_p_chunks_tmem<2, 0, 2, true, true>(s, sl2, m_run, tP, acc, mx);
+      softmax_p_chunks_tmem<2, 0, 2, kEmuPairs, true>(s, sl2, m_run, tP, acc, mx);
     else
-      softmax_p_chunks_tmem<2, 0, 2, false, true>(s, sl2, m_run, tP, acc, mx);
+      softmax_p_chunks_tmem<2, 0, 2, 0, true>(s, sl2, m_run, tP, acc, mx);
     const float m_blk = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * sl2;
     const bool jump = m_blk > m_run + kRescaleThreshold;
     if (__any_sync(0xffffffffu, jump)) {
@@ -235,7 +246,7 @@ __device__ __forceinline__ float softmax_half_tmem(uint32_t (&s)[2][32], int lim
       tmem_wait_st();  // the first pass's stores land before they are overwritten
 #pragma unroll
       for (int k = 0; k < 4; ++k) acc[k] = make_float2(0.f, 0.f);
-      softmax_p_chunks_tmem<2, 0, 2, false, false>(s, sl2, m_run, tP, acc, mx);
+      softmax_p_chunks_tmem<2, 0, 2, 0, false>(s, sl2, m_run, tP, acc, mx);
     }
   } else {
 #pragma unroll
@@ -254,7 +265,7 @@ __device__ __forceinline__ float softmax_half_tmem(uint32_t (&s)[2][32], int lim
       m_run = m_new;
     }
     const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-    softmax_p_chunks_tmem<2, 0, 2, false, false>(s, sl2, m_use, tP, acc, mx);
+    softmax_p_chunks_tmem<2, 0, 2, 0, false>(s, sl2, m_use, tP, acc, mx);
   }
   const float2 r2 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
   hsum = r2.x + r2.y;

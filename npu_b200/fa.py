@@ -69,6 +69,13 @@ class NpuAttention:
         assert len(start_rows) == N_in
         home = Q_stack.device
         dev = self._dev(Q_stack)
+        if not Q_stack.is_cuda:
+            # Host stacks (the reference's case): b2a_prefill_host uploads,
+            # computes and downloads in overlapping chunks.
+            q, k, v = (t.to(torch.bfloat16).contiguous().unsqueeze(1) for t in (Q_stack, K_stack, V_stack))
+            o = api.prefill_host(q, k, v, start_pos_per_batch=[int(r) for r in start_rows], causal=causal,
+                                 out_dtype=self.out_dtype, device=dev)
+            return o.squeeze(1)
         q = Q_stack.to(device=dev, dtype=torch.bfloat16, non_blocking=True).unsqueeze(1)
         k = K_stack.to(device=dev, dtype=torch.bfloat16, non_blocking=True).unsqueeze(1)
         v = V_stack.to(device=dev, dtype=torch.bfloat16, non_blocking=True).unsqueeze(1)

@@ -177,3 +177,52 @@ def test_qk_norm_rope_append_argument_validation():
     if not torch.cuda.is_available():
         assert _qk_rope() in (_lib.B2A_ERR_CUDA, _lib.B2A_ERR_DEVICE)
         assert _qk_rope(rd=0, cos=None, sin=None, qn=None, kn=None) in (_lib.B2A_ERR_CUDA, _lib.B2A_ERR_DEVICE)
+
+
+def _a256(x):
+    return (x + 255) // 256 * 256
+
+
+def test_prefill_host_workspace_arithmetic():
+    lib = _lib.load()
+    # Config 3 geometry; the default 32 chunks hold 2 whole batches each:
+    # 2 slots of q/k/v/o + B ints.
+    B, Hq, Hkv, T, D = 64, 32, 4, 8192, 128
+    per = 2 * Hkv  # units per chunk
+    slot = _a256(per * 8 * T * D * 2) + 2 * _a256(per * T * D * 2) + _a256(per * 8 * T * D * 2)
+    assert lib.b2a_prefill_host_workspace_bytes(B, Hq, Hkv, T, T, D, 0, 0) == 2 * slot + _a256(B * 4)
+    assert lib.b2a_prefill_host_workspace_bytes(B, Hq, Hkv, T, T, D, 0, 32) == 2 * slot + _a256(B * 4)
+    # 16 chunks of 4 batches, fp32 output (o region doubled).
+    per = 4 * Hkv
+    slot32 = _a256(per * 8 * T * D * 2) + 2 * _a256(per * T * D * 2) + _a256(per * 8 * T * D * 4)
+    assert lib.b2a_prefill_host_workspace_bytes(B, Hq, Hkv, T, T, D, 1, 16) == 2 * slot32 + _a256(B * 4)
+    # One batch, fewer units than chunks: chunks are single KV heads.
+    one = _a256(8 * 512 * 64 * 2) + 2 * _a256(512 * 64 * 2) + _a256(8 * 512 * 64 * 2)
+    assert lib.b2a_prefill_host_workspace_bytes(1, 32, 4, 512, 512, 64, 0, 0) == 2 * one + 256
+    for bad in ((0, 8, 2, 64, 64, 128, 0, 0), (1, 8, 3, 64, 64, 128, 0, 0), (1, 8, 2, 64, 64, 96, 0, 0),
+                (1, 8, 2, 0, 64, 128, 0, 0), (1, 8, 2, 64, -1, 128, 0, 0), (1, 8, 2, 64, 64, 128, 0, -1)):
+        assert lib.b2a_prefill_host_workspace_bytes(*bad) == 0, bad
+
+
+def test_prefill_host_argument_validation():
+    lib = _lib.load()
+
+    def call(**over):
+        a = dict(q=FAKE, k=FAKE, v=FAKE, o=FAKE, B=2, Hq=8, Hkv=2, Tq=64, Tk=64, D=128, sp=0, spb=None,
+                 scale=0.125, causal=1, fp32=0, n=0, ws=FAKE * 16, wsb=1 << 30)
+        a.update(over)
+        return lib.b2a_prefill_host(a["q"], a["k"], a["v"], a["o"], a["B"], a["Hq"], a["Hkv"], a["Tq"],
+                                    a["Tk"], a["D"], a["sp"], a["spb"], a["scale"], a["causal"], a["fp32"],
+                                    a["n"], a["ws"], a["wsb"], None)
+
+    assert call(D=96) == _lib.B2A_ERR_HEAD_DIM
+    assert call(Hkv=3) == _lib.B2A_ERR_GQA
+    assert call(B=0) == _lib.B2A_ERR_INVALID_ARG
+    assert call(q=None) == _lib.B2A_ERR_INVALID_ARG
+    assert call(k=None) == _lib.B2A_ERR_INVALID_ARG
+    assert call(scale=0.0) == _lib.B2A_ERR_INVALID_ARG
+    assert call(ws=None) == _lib.B2A_ERR_WORKSPACE
+    assert call(wsb=1024) == _lib.B2A_ERR_WORKSPACE
+    assert call(ws=FAKE * 16 + 16) == _lib.B2A_ERR_WORKSPACE  # workspace must be 256-byte aligned
+    if not torch.cuda.is_available():
+        assert call() in (_lib.B2A_ERR_CUDA, _lib.B2A_ERR_DEVICE)
