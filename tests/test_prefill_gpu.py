@@ -249,6 +249,33 @@ def test_no_device_error_left(cuda_dev):
     assert api.device_error(clear=True) == 0
 
 
+def test_d256_per_batch_starts_ragged_pairs_and_lse(cuda_dev):
+    """Head dim 256 (256-row query pairs on SM pairs): per-batch start
+    positions including a negative one (leading rows fully masked), a query
+    length that leaves the second tile of the last pair partly and wholly
+    past Tq, LSE."""
+    from npu_b200 import api
+
+    g = torch.Generator().manual_seed(21)
+    for Tq in (300, 100):
+        B, Hq, Hkv, Tk, D = 3, 4, 2, 520, 256
+        q, k, v = _rand((B, Hq, Tq, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev)
+        sps = [-40, 0, Tk - Tq]
+        out, lse = api.prefill(q, k, v, start_pos_per_batch=torch.tensor(sps, dtype=torch.int32, device=cuda_dev),
+                               return_lse=True)
+        for b, sp in enumerate(sps):
+            ref = A.dense_attention(q[b:b + 1].cpu(), k[b:b + 1].cpu(), v[b:b + 1].cpu(), start_pos=sp)
+            assert (out[b:b + 1].cpu() - ref).abs().max().item() <= TOL, (Tq, b)
+            s = (q[b].float().cpu() @ A.expand_kv(k[b:b + 1].cpu().float(), 2)[0].transpose(-1, -2)) / math.sqrt(D)
+            s = s.masked_fill(A.causal_mask(Tq, Tk, sp), float("-inf"))
+            ref_lse = torch.logsumexp(s, dim=-1)
+            got = lse[b].cpu()
+            live = torch.isfinite(ref_lse)
+            assert torch.all(torch.isneginf(got[~live]))
+            assert (got[live] - ref_lse[live]).abs().max().item() < 1e-3, (Tq, b)
+        assert torch.all(out[0, :, :40] == 0)
+
+
 def test_config5_geometry_sampled_rows(cuda_dev):
     """Config 5 head geometry (16 query / 2 KV heads, D=256, scale 1/16) on a
     16k-token causal prefill: sampled rows against the oracle."""
