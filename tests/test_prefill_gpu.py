@@ -250,10 +250,9 @@ def test_no_device_error_left(cuda_dev):
 
 
 def test_d256_per_batch_starts_ragged_pairs_and_lse(cuda_dev):
-    """Head dim 256 (256-row query pairs on SM pairs): per-batch start
-    positions including a negative one (leading rows fully masked), a query
-    length that leaves the second tile of the last pair partly and wholly
-    past Tq, LSE."""
+    """Head dim 256: per-batch start positions including a negative one
+    (leading rows fully masked), query lengths that end inside a 128-row
+    tile (300) or below one tile (100), and the LSE."""
     from npu_b200 import api
 
     g = torch.Generator().manual_seed(21)
