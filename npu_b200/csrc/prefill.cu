@@ -7,7 +7,7 @@
 namespace b2a {
 
 #ifndef B2A_ONE_TILE_MAX_ROWS
-#define B2A_ONE_TILE_MAX_ROWS 512
+#define B2A_ONE_TILE_MAX_ROWS 1024
 #endif
 // Longest query length served by one-tile CTAs (prefill_rows_per_cta).
 constexpr int kOneTileMaxRows = B2A_ONE_TILE_MAX_ROWS;
