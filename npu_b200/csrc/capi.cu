@@ -364,13 +364,23 @@ int b2a_version(void) { return 100; }
 
 int b2a_decode_default_split(int B, int Hkv, int Lmax) {
   if (B <= 0 || Hkv <= 0 || Lmax <= 0) return 512;
-  // Aim for ~8 waves of 2 CTAs per SM on 148 SMs assuming an average length of
-  // Lmax / 2, clamped so a split is neither launch-bound nor a long tail.
-  long long want = ((long long)B * Hkv * Lmax) / (2LL * 148 * 2 * 8);
-  want = (want + 63) / 64 * 64;
-  if (want < 512) want = 512;
-  if (want > 4096) want = 4096;
-  return (int)want;
+  // Keys x KV heads to stream, assuming caches half full (lengths are on the
+  // device), spread over about one wave of CTAs (two per SM on 148 SMs).
+  // Measured on B200 (config 4 heads, D = 128): each split CTA pays a fixed
+  // cost (pipeline fill, its partial O and LSE, one more input to the
+  // combine), so few long splits beat many short ones. A split that leaves a
+  // few CTAs for a second, nearly empty wave is much slower: at 16
+  // sequences 4096 keys ran 5.9 TB/s, 3072 4.8 and 512 4.6. The measured
+  // optima sat at powers of two, hence the rounding. With several waves of
+  // work anyway, 2048 is best (128 sequences: 6.85 TB/s against 6.74 at
+  // 4096).
+  const long long slots = 2LL * 148;
+  const long long work = (long long)B * Hkv * ((Lmax + 1) / 2);
+  const long long want = work / slots;
+  int split = 512;
+  while (split < 4096 && (long long)split * 3 / 2 < want) split *= 2;  // nearest power of two
+  if (split > 2048 && work / 2048 >= 4 * slots) split = 2048;
+  return split;
 }
 
 size_t b2a_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int Lmax, int split_len) {
