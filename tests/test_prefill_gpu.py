@@ -275,6 +275,39 @@ def test_d256_per_batch_starts_ragged_pairs_and_lse(cuda_dev):
         assert torch.all(out[0, :, :40] == 0)
 
 
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_two_tile_items_without_keys_and_chunked_batches(cuda_dev, out_dtype):
+    """Two-tile CTAs (Tq > 1024) over 2 x 48 heads x 5 query blocks with
+    per-batch start positions: query blocks with no visible key at all
+    (batch 0, start -500: the first block), blocks where only the second
+    128-row tile sees keys (the second block), a chunked batch (start 200,
+    Tq < Tk), the LSE, and the same geometry without the causal mask; all
+    compared in full against the oracle."""
+    from npu_b200 import api
+
+    g = torch.Generator().manual_seed(31)
+    B, Hq, Hkv, Tq, Tk, D = 2, 48, 8, 1100, 1300, 128
+    q, k, v = _rand((B, Hq, Tq, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev)
+    sps = [-500, 200]
+    out, lse = api.prefill(q, k, v, start_pos_per_batch=torch.tensor(sps, dtype=torch.int32, device=cuda_dev),
+                           out_dtype=out_dtype, return_lse=True)
+    assert api.device_error() == 0
+    for b, sp in enumerate(sps):
+        ref = A.dense_attention(q[b:b + 1].cpu(), k[b:b + 1].cpu(), v[b:b + 1].cpu(), start_pos=sp)
+        assert (out[b:b + 1].float().cpu() - ref).abs().max().item() <= TOL, b
+        s = (q[b].float().cpu() @ A.expand_kv(k[b:b + 1].cpu().float(), Hq // Hkv)[0].transpose(-1, -2)) / math.sqrt(D)
+        s = s.masked_fill(A.causal_mask(Tq, Tk, sp), float("-inf"))
+        ref_lse = torch.logsumexp(s, dim=-1)
+        live = torch.isfinite(ref_lse)
+        assert torch.all(torch.isneginf(lse[b].cpu()[~live]))
+        assert (lse[b].cpu()[live] - ref_lse[live]).abs().max().item() < 1e-3, b
+    assert torch.all(out[0, :, :500] == 0)
+    # Non-causal, same geometry: every item has all key blocks.
+    out2 = api.prefill(q, k, v, causal=False, out_dtype=out_dtype)
+    ref2 = A.dense_attention(q.cpu(), k.cpu(), v.cpu(), causal=False)
+    assert (out2.float().cpu() - ref2).abs().max().item() <= TOL
+
+
 def test_config5_geometry_sampled_rows(cuda_dev):
     """Config 5 head geometry (16 query / 2 KV heads, D=256, scale 1/16) on a
     16k-token causal prefill: sampled rows against the oracle."""
