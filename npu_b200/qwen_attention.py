@@ -16,6 +16,10 @@ Here:
     [B, T, Hq * D] layout the output projection takes (no transpose copy);
   * the output projection is a cuBLAS GEMM.
 The gate is read in place from the q projection (a strided view).
+
+`attn_forward` at the end of this file keeps the reference function's own
+signature and tuple cache of expanded heads (a one-import drop-in for
+qwen/forward.py) and runs the same attention kernels on that cache.
 """
 from __future__ import annotations
 
@@ -118,3 +122,94 @@ class QwenGatedAttentionB200:
     def forward(self, x: torch.Tensor, cache: KVCache, layer: int = 0) -> torch.Tensor:
         """attn_forward's output [B, T, d_model] (before the residual add)."""
         return F.linear(self.attention(x, cache, layer), self.wo)
+
+
+_LAYER_WEIGHTS: dict = {}
+
+
+def _layer_on_device(layer, device: torch.device, dtype: torch.dtype) -> dict:
+    """The layer's attention weights on `device` in `dtype`: the tensors
+    themselves when they already are, else copies made on first use and kept
+    per layer object (later in-place changes to the layer's host weights are
+    not seen)."""
+    names = ("attn_norm", "wq", "wk", "wv", "wo", "q_norm", "k_norm")
+    if all(getattr(layer, n).device == device and getattr(layer, n).dtype == dtype for n in names):
+        return {n: getattr(layer, n) for n in names}
+    key = (id(layer), str(device), dtype)
+    ent = _LAYER_WEIGHTS.get(key)
+    if ent is None or ent["layer"] is not layer:
+        ent = {n: getattr(layer, n).to(device=device, dtype=dtype).contiguous() for n in names}
+        ent["layer"] = layer
+        _LAYER_WEIGHTS[key] = ent
+    return ent
+
+
+@torch.no_grad()
+def attn_forward(x: torch.Tensor, layer, cfg, cos: torch.Tensor, sin: torch.Tensor, kv_cache, start_pos: int,
+                 device: Optional[torch.device] = None):
+    """Drop-in for the reference's attn_forward (qwen/forward.py:133-239):
+    same arguments (x [B, T, d_model]; `layer` with attn_norm, wq holding
+    [q_h | gate_h] per head, wk, wv, wo, q_norm, k_norm; `cfg` with n_head,
+    n_head_kv, head_dim, rope_dim, rms_eps; the cos / sin tables of
+    build_partial_rope_cache; the (k, v) cache of expanded heads [B, Tk,
+    n_head, head_dim] or None; the absolute position of x's first token) and
+    the same results: the block output [B, T, d_model] on x's device and dtype,
+    and the new (k, v) cache, grown by torch.cat as in the reference.
+
+    Projections, the per-head Q/K RMSNorm, the partial RoPE and the cache
+    concatenation run as torch ops on `device` (default: the current CUDA
+    device), in x's dtype as in the reference. The attention itself runs on
+    the B200 kernels with the sigmoid gate fused into their output stores:
+    b2a_prefill_gated for T > 1 (causal from start_pos), b2a_decode_gated for
+    T = 1 (every cached key, no mask, qwen/forward.py:211-216). The kernels read
+    one copy of each KV head from the expanded cache (a head stride of
+    n_head / n_head_kv heads), so GQA costs no extra cache traffic. The
+    returned cache lives on `device` as bf16 (the kernels' input type); a
+    caller passes it back unchanged, as the reference's forward does."""
+    if device is None:
+        if not torch.cuda.is_available():
+            raise RuntimeError("attn_forward needs a CUDA device (no CPU path)")
+        device = torch.device("cuda", torch.cuda.current_device())
+    B, T, _ = x.shape
+    Hq, Hkv, Dh, rd = cfg.n_head, cfg.n_head_kv, cfg.head_dim, cfg.rope_dim
+    rep = Hq // Hkv
+    dtype = x.dtype if x.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    w = _layer_on_device(layer, device, dtype)
+    xd = x.to(device=device, dtype=dtype)
+    h = _rms_norm(xd, w["attn_norm"], cfg.rms_eps)
+    q_full = F.linear(h, w["wq"]).view(B, T, Hq, 2, Dh)
+    q, q_gate = q_full[..., 0, :], q_full[..., 1, :]
+    k = F.linear(h, w["wk"]).view(B, T, Hkv, Dh)
+    v = F.linear(h, w["wv"]).view(B, T, Hkv, Dh)
+    q = _rms_norm(q, w["q_norm"], cfg.rms_eps)
+    k = _rms_norm(k, w["k_norm"], cfg.rms_eps)
+    cs = cos[start_pos:start_pos + T].to(device=device, dtype=dtype)
+    sn = sin[start_pos:start_pos + T].to(device=device, dtype=dtype)
+
+    def rope(t):  # qwen/forward.py:81-95: rotate-half on the first rd lanes
+        tr, tp = t[..., :rd], t[..., rd:]
+        half = rd // 2
+        rot = torch.cat([-tr[..., half:], tr[..., :half]], dim=-1)
+        return torch.cat([tr * cs[None, :, None, :] + rot * sn[None, :, None, :], tp], dim=-1)
+
+    q, k = rope(q), rope(k)
+    k = k.to(torch.bfloat16).repeat_interleave(rep, dim=2)
+    v = v.to(torch.bfloat16).repeat_interleave(rep, dim=2)
+    if kv_cache is not None:
+        k = torch.cat([kv_cache[0].to(device=device, dtype=torch.bfloat16), k], dim=1)
+        v = torch.cat([kv_cache[1].to(device=device, dtype=torch.bfloat16), v], dim=1)
+    Tk = k.shape[1]
+    # One copy of each KV head: heads 0, rep, 2 rep, ... of the expanded cache.
+    kh = k[:, :, ::rep].transpose(1, 2)   # [B, Hkv, Tk, Dh], strided view
+    vh = v[:, :, ::rep].transpose(1, 2)
+    qb = q.to(torch.bfloat16)
+    out = torch.empty((B, T, Hq, Dh), dtype=dtype, device=device)
+    if T == 1:
+        seqlens = torch.full((B,), Tk, dtype=torch.int32, device=device)
+        api.decode(qb[:, 0], kh, vh, seqlens, scale=1.0 / math.sqrt(Dh), out_dtype=dtype, out=out[:, 0],
+                   gate=q_gate[:, 0])
+    else:
+        api.prefill(qb.transpose(1, 2), kh, vh, start_pos=start_pos, scale=1.0 / math.sqrt(Dh), causal=True,
+                    out_dtype=dtype, out=out.transpose(1, 2), gate=q_gate.transpose(1, 2))
+    y = F.linear(out.view(B, T, Hq * Dh), w["wo"])
+    return y.to(device=x.device, dtype=x.dtype), (k, v)

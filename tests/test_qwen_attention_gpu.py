@@ -80,3 +80,38 @@ def test_qwen_gated_attention_prefill_then_decode(cuda_dev):
     assert cache.lengths() == [pos, pos]
     from npu_b200 import api
     assert api.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_attn_forward_drop_in_matches_reference_signature(cuda_dev, dtype):
+    """npu_b200.qwen_attention.attn_forward called exactly as qwen/forward.py
+    calls its own attn_forward (host tensors, the reference layer object and
+    config, cos/sin tables, a tuple cache of expanded heads grown step by
+    step): a 300-token prefill from position 0, then four one-token decode
+    steps feeding the returned cache back in."""
+    from npu_b200.qwen_attention import attn_forward
+
+    rc = R.QwenAttnConfig()
+    layer = R.make_layer(rc, seed=9, dtype=dtype)
+    cos, sin = R.partial_rope_tables(rc.rope_dim, 1024, rc.rope_theta, dtype)
+    g = torch.Generator().manual_seed(10)
+    B, T = 2, 300
+    x = torch.randn(B, T, rc.d_model, generator=g).to(dtype)
+    ref, ref_cache = R.attn_forward(x, layer, rc, cos, sin, None, 0)
+    out, cache = attn_forward(x, layer, rc, cos, sin, None, 0, device=cuda_dev)
+    assert out.device == x.device and out.dtype == x.dtype and out.shape == ref.shape
+    scale = max(1.0, ref.float().abs().max().item())
+    assert (out.float() - ref.float()).abs().max().item() <= TOL * scale
+    assert cache[0].shape == ref_cache[0].shape and cache[1].shape == ref_cache[1].shape
+    pos = T
+    for step in range(4):
+        xs = torch.randn(B, 1, rc.d_model, generator=g).to(dtype)
+        ref, ref_cache = R.attn_forward(xs, layer, rc, cos, sin, ref_cache, pos)
+        out, cache = attn_forward(xs, layer, rc, cos, sin, cache, pos, device=cuda_dev)
+        scale = max(1.0, ref.float().abs().max().item())
+        assert (out.float() - ref.float()).abs().max().item() <= TOL * scale, step
+        pos += 1
+    assert cache[0].shape == ref_cache[0].shape == (B, pos, rc.n_head, rc.head_dim)
+    for mine, theirs in zip(cache, ref_cache):
+        assert mine.shape == theirs.shape
+        assert (mine.float().cpu() - theirs.float()).abs().max().item() < 5e-2 * max(1.0, theirs.float().abs().max())
