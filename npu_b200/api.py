@@ -2,8 +2,9 @@
 and the fused RoPE + KV-cache append that feeds them.
 
 These are the B200 entry points behind the reference-compatible wrapper in
-npu_b200.fa (NpuAttention.run_batch). Tensors must already be CUDA bf16 with a
-contiguous head dimension; nothing here falls back to a CPU path.
+npu_b200.fa (NpuAttention.run_batch). Tensors are CUDA bf16 with a contiguous
+head dimension, except for prefill_host, which takes host bf16 tensors and
+moves them itself; nothing here falls back to a CPU path.
 """
 from __future__ import annotations
 
@@ -163,21 +164,23 @@ def prefill_host(
         raise ValueError("out_dtype must be float32 or bfloat16")
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    if out is None:
-        out = torch.empty((B, Hq, Tq, D), dtype=out_dtype, pin_memory=True)
-    elif (out.is_cuda or out.dtype != out_dtype or tuple(out.shape) != (B, Hq, Tq, D)
-          or not out.is_contiguous()):
+    if out is not None and (out.is_cuda or out.dtype != out_dtype or tuple(out.shape) != (B, Hq, Tq, D)
+                            or not out.is_contiguous()):
         raise ValueError("out must be a contiguous CPU tensor [B, Hq, Tq, D] of out_dtype")
     spb = None
     if start_pos_per_batch is not None:
+        if isinstance(start_pos_per_batch, torch.Tensor) and start_pos_per_batch.is_cuda:
+            raise ValueError("start_pos_per_batch must be on the host")
         spb = torch.as_tensor(start_pos_per_batch, dtype=torch.int32).contiguous()
-        if spb.is_cuda or spb.numel() != B:
+        if spb.numel() != B:
             raise ValueError("start_pos_per_batch must be a host sequence of B int32 positions")
     if device is None:
         if not torch.cuda.is_available():
             raise RuntimeError("prefill_host needs a CUDA device (no CPU path)")
         device = torch.device("cuda", torch.cuda.current_device())
     device = torch.device(device)
+    if out is None:
+        out = torch.empty((B, Hq, Tq, D), dtype=out_dtype, pin_memory=True)
     out_fp32 = out_dtype == torch.float32
     lib = _lib.load()
     need = int(lib.b2a_prefill_host_workspace_bytes(B, Hq, Hkv, Tq, Tk, D, 1 if out_fp32 else 0, n_chunks))

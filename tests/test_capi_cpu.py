@@ -226,3 +226,30 @@ def test_prefill_host_argument_validation():
     assert call(ws=FAKE * 16 + 16) == _lib.B2A_ERR_WORKSPACE  # workspace must be 256-byte aligned
     if not torch.cuda.is_available():
         assert call() in (_lib.B2A_ERR_CUDA, _lib.B2A_ERR_DEVICE)
+
+
+def test_prefill_host_python_argument_checks():
+    """npu_b200.api.prefill_host validates its host tensors before touching
+    CUDA: device tensors, other dtypes, non-contiguous or mismatched shapes,
+    and start positions of the wrong length are refused."""
+    from npu_b200 import api
+
+    q = torch.zeros(2, 4, 16, 64, dtype=torch.bfloat16)
+    k = torch.zeros(2, 2, 16, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        api.prefill_host(q.float(), k, k)
+    with pytest.raises(ValueError):
+        api.prefill_host(q.transpose(1, 2), k, k)  # not contiguous
+    with pytest.raises(ValueError):
+        api.prefill_host(q, k[:, :, :8], k)        # k / v shapes differ
+    with pytest.raises(ValueError):
+        api.prefill_host(q, k[:1], k[:1])          # batch mismatch
+    with pytest.raises(ValueError):
+        api.prefill_host(q, k, k, out_dtype=torch.float16)
+    with pytest.raises(ValueError):
+        api.prefill_host(q, k, k, start_pos_per_batch=[0, 1, 2])
+    with pytest.raises(ValueError):
+        api.prefill_host(q, k, k, out=torch.empty(2, 4, 16, 64, dtype=torch.float32))  # out dtype
+    if not torch.cuda.is_available():
+        with pytest.raises(RuntimeError):
+            api.prefill_host(q, k, k)  # no device: no CPU path
