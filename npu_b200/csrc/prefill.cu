@@ -80,11 +80,29 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
     for (int t = 0; t < C::NQT; ++t) mbar_init(&bars->drain[t], 1);
     bars->abort_flag = 0;
     fence_mbar_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tm_q);
-    tma_prefetch_desc(&tm_k);
-    tma_prefetch_desc(&tm_v);
+    // The Q tiles and the first ring of K/V tiles are requested here, so
+    // their latency overlaps the TMEM allocation and the block barrier below
+    // (the producer warp issues the rest). The ring slots are all free.
+    if (n_kv > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_arrive_expect_tx(&bars->q_full, C::NQT * C::Q_TILE_BYTES);
+#pragma unroll
+      for (int t = 0; t < C::NQT; ++t)
+#pragma unroll
+        for (int c = 0; c < C::KCH; ++c)
+          tma_load_4d(sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, &tm_q, &bars->q_full, c * 64,
+                      q0 + t * C::BM, h, b);
+      for (int i = 0; i < min(C::STAGES, 2 * n_kv); ++i) {
+        uint8_t* dst = sKV + i * C::KV_TILE_BYTES;
+        mbar_arrive_expect_tx(&bars->kv_full[i], C::KV_TILE_BYTES);
+#pragma unroll
+        for (int c = 0; c < C::KCH; ++c)
+          tma_load_4d(dst + c * C::CHUNK_BYTES, (i & 1) ? &tm_v : &tm_k, &bars->kv_full[i], c * 64,
+                      (i >> 1) * C::BN, hk, b);
+      }
+    }
   }
   if (warp == 1) {
     tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
@@ -104,15 +122,9 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
   // helpers), which keeps the operands in uniform registers.
   if (n_kv > 0 && warp == 0) {
     // ------------------------------------------------------------ producer
-    mbar_arrive_expect_tx_w(&bars->q_full, C::NQT * C::Q_TILE_BYTES);
-#pragma unroll
-    for (int t = 0; t < C::NQT; ++t)
-#pragma unroll
-      for (int c = 0; c < C::KCH; ++c)
-        tma_load_4d_w(sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, &tm_q, &bars->q_full, c * 64, q0 + t * C::BM,
-                      h, b);
-    int issued = 0;
-    for (int i = 0; i < 2 * n_kv; ++i) {
+    // Q and the first STAGES K/V tiles were requested during set-up.
+    int issued = min(C::STAGES, 2 * n_kv);
+    for (int i = issued; i < 2 * n_kv; ++i) {
       const int slot = i % C::STAGES;
       const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->kv_empty[slot], ph ^ 1u, abort_flag, p.err))) break;
