@@ -4,9 +4,10 @@
 // npu/fa.py:266-311, runs, and syncs and reads O back, :313-323). The problem
 // is cut into chunks of (batch, KV head) units; each chunk's Q/K/V go
 // host -> device on one copy stream, the prefill kernel runs on the caller's
-// stream, and the output goes device -> host on a second copy stream. Two device slots alternate between chunks, so chunk i+1's upload and
-// chunk i-1's download run while chunk i computes; upload and download use
-// the two directions of the host link at the same time.
+// stream, and the output goes device -> host on a second copy stream. Two
+// device slots alternate between chunks, so chunk i+1's upload and chunk
+// i-1's download run while chunk i computes; upload and download use the two
+// directions of the host link at the same time.
 //
 // Stream protocol (all waits are stream-side, nothing blocks the host):
 //   fork        recorded on the caller's stream; both copy streams wait on it
