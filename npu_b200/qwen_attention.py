@@ -24,6 +24,7 @@ qwen/forward.py) and runs the same attention kernels on that cache.
 from __future__ import annotations
 
 import math
+import weakref
 from dataclasses import dataclass
 from typing import Optional
 
@@ -124,24 +125,32 @@ class QwenGatedAttentionB200:
         return F.linear(self.attention(x, cache, layer), self.wo)
 
 
+# Device copies of layers' attention weights, by id() of the layer object and
+# dropped when that object is collected (layer classes such as dataclasses
+# are not hashable, so a weak-key dictionary cannot hold them).
 _LAYER_WEIGHTS: dict = {}
 
 
 def _layer_on_device(layer, device: torch.device, dtype: torch.dtype) -> dict:
     """The layer's attention weights on `device` in `dtype`: the tensors
     themselves when they already are, else copies made on first use and kept
-    per layer object (later in-place changes to the layer's host weights are
-    not seen)."""
+    while the layer object lives (later in-place changes to the layer's host
+    weights are not seen)."""
     names = ("attn_norm", "wq", "wk", "wv", "wo", "q_norm", "k_norm")
     if all(getattr(layer, n).device == device and getattr(layer, n).dtype == dtype for n in names):
         return {n: getattr(layer, n) for n in names}
-    key = (id(layer), str(device), dtype)
-    ent = _LAYER_WEIGHTS.get(key)
-    if ent is None or ent["layer"] is not layer:
-        ent = {n: getattr(layer, n).to(device=device, dtype=dtype).contiguous() for n in names}
-        ent["layer"] = layer
-        _LAYER_WEIGHTS[key] = ent
-    return ent
+    lid = id(layer)
+    per_layer = _LAYER_WEIGHTS.get(lid)
+    if per_layer is None:
+        per_layer = _LAYER_WEIGHTS[lid] = {}
+        try:
+            weakref.finalize(layer, _LAYER_WEIGHTS.pop, lid, None)
+        except TypeError:  # not weak-referenceable: the copies live until exit
+            pass
+    key = (str(device), dtype)
+    if key not in per_layer:
+        per_layer[key] = {n: getattr(layer, n).to(device=device, dtype=dtype).contiguous() for n in names}
+    return per_layer[key]
 
 
 @torch.no_grad()
