@@ -95,7 +95,14 @@ B2A_API int b2a_prefill(const void* q, const void* k, const void* v, void* o, fl
  */
 B2A_API size_t b2a_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int Lmax, int split_len);
 
-/* The split length b2a_decode uses when called with split_len = 0. */
+/*
+ * The split length b2a_decode uses when called with split_len = 0: keys per
+ * split CTA such that the estimated work (B x Hkv x Lmax / 2 keys, since the
+ * lengths are on the device) fills about one wave of CTAs, rounded to a
+ * power of two in [512, 4096], and 2048 when that still leaves several
+ * waves. Pass an explicit split_len when the lengths are known to be far
+ * from half the cache.
+ */
 B2A_API int b2a_decode_default_split(int B, int Hkv, int Lmax);
 
 /*
