@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Headline (`value`): causal GQA prefill attention throughput, algorithmic
-TFLOP/s, on BASELINE config 3 at T=8192 (B=64, Hq=32, Hkv=4, D=128, bf16,
+TFLOP/s, on config 3 at T=8192 (B=64, Hq=32, Hkv=4, D=128, bf16,
 scale 1/sqrt(128)); the (batch x KV-head) units are split across the N GPUs
 with no collective (strong scaling: total work fixed). A step is one launch
 over the whole batch. `decode` reports config 4 (128 sequences, one query

@@ -160,10 +160,14 @@ B2A_API int b2a_decode_gated(const void* q, const void* k_cache, const void* v_c
  * pointers). No counterpart in the reference.
  * Same arguments and results as b2a_decode minus the workspace. Scratch is a
  * device array of B2A_NOALLOC_SCRATCH_BYTES inside this library, held by every
- * GPU that loads it until exit; problems needing more return
- * B2A_ERR_WORKSPACE (use a larger split_len, or b2a_decode). The first call on
- * a device looks up the array's device address (cudaGetSymbolAddress): make
- * it outside any stream capture. All calls on a device share the buffer, so
+ * GPU that loads it until exit. With split_len = 0 the default split length
+ * is doubled until the partial results fit; problems that need more even with
+ * one split per sequence (or with the caller's split_len) return
+ * B2A_ERR_WORKSPACE before any launch (use a larger split_len, or b2a_decode).
+ * A non-sm_100 device returns B2A_ERR_DEVICE. The first call in a device's
+ * context looks up the array's device address (cudaGetSymbolAddress): make it
+ * outside any stream capture; a new context (after cudaDeviceReset) is
+ * detected and looked up again. All calls on a device share the buffer, so
  * calls that overlap on the GPU race; nothing in it needs to start at zero.
  */
 B2A_API int b2a_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const int* seqlens,

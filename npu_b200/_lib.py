@@ -26,6 +26,10 @@ B2A_ERR_DEVICE_TIMEOUT = -9
 B2A_ERR_DEVICE_BAD_LEN = -10
 B2A_ERR_CUDA = -11
 
+# Size of the fixed device scratch behind b2a_decode_noalloc
+# (B2A_NOALLOC_SCRATCH_BYTES in include/b2attn.h).
+B2A_NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024
+
 _c_ll3 = ctypes.c_longlong * 3
 _c_ll2 = ctypes.c_longlong * 2
 

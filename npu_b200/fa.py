@@ -9,6 +9,15 @@ argument meaning, preconditions (npu/fa.py:220-223) and bf16 result — and runs
 every block on the sm_100a prefill kernel. Block n is an independent problem
 whose query row r sits at absolute position start_rows[n] + r; there is no
 per-dispatch static state and no xclbin cache to key.
+
+The reference caller builds its stacks in one fixed order (smollm.py:157-161):
+for every (batch, head) unit, its n_q query blocks in row order with start
+rows s0, s0 + BR, ..., and a full copy of the unit's K/V for each block.
+run_batch recognises that layout (start rows, and K/V equal across a unit's
+blocks) and then runs one prefill per unit over all n_q * BR rows with one
+copy of K/V: n_q times fewer K/V bytes uploaded and converted, and full
+128-row query tiles even when BR is smaller. Any other stack is run block by
+block.
 """
 from __future__ import annotations
 
@@ -69,6 +78,9 @@ class NpuAttention:
         assert len(start_rows) == N_in
         home = Q_stack.device
         dev = self._dev(Q_stack)
+        n_q = self._units_of_blocks(K_stack, V_stack, start_rows)
+        if n_q > 1:
+            return self._run_units(Q_stack, K_stack, V_stack, int(start_rows[0]), n_q, causal, dev, home)
         if not Q_stack.is_cuda:
             # Host stacks (the reference's case): b2a_prefill_host uploads,
             # computes and downloads in overlapping chunks.
@@ -83,6 +95,45 @@ class NpuAttention:
         o = api.prefill(q.contiguous(), k.contiguous(), v.contiguous(), start_pos_per_batch=sp,
                         causal=causal, out_dtype=self.out_dtype)
         o = o.squeeze(1)
+        return o if home == o.device else o.to(home)
+
+    def _units_of_blocks(self, K_stack: torch.Tensor, V_stack: torch.Tensor, start_rows: Sequence[int]) -> int:
+        """n_q > 1 if the stacks hold units of n_q consecutive query blocks in
+        the reference caller's order (block i of a unit starts at s0 + i * BR,
+        the same s0 for every unit) whose K/V blocks are identical within the
+        unit; else 1."""
+        N, BR = len(start_rows), self.BR
+        if N < 2:
+            return 1
+        rows = [int(r) for r in start_rows]
+        s0 = rows[0]
+        n_q = 1
+        while n_q < N and rows[n_q] == s0 + n_q * BR:
+            n_q += 1
+        if n_q < 2 or N % n_q or any(rows[n] != s0 + (n % n_q) * BR for n in range(N)):
+            return 1
+        U = N // n_q
+        for t in (K_stack, V_stack):
+            t4 = t.view(U, n_q, *t.shape[1:]) if t.is_contiguous() else t.reshape(U, n_q, *t.shape[1:])
+            if not torch.equal(t4, t4[:, :1].expand_as(t4)):
+                return 1
+        return n_q
+
+    def _run_units(self, Q_stack, K_stack, V_stack, s0: int, n_q: int, causal: bool, dev, home):
+        """One prefill per (batch, head) unit: its n_q blocks' rows as one query
+        sequence [n_q * BR] from position s0, against one copy of its K/V."""
+        N, BR, D = Q_stack.shape
+        TK = K_stack.shape[1]
+        U = N // n_q
+        q = Q_stack.reshape(U, 1, n_q * BR, D)
+        k = K_stack.reshape(U, n_q, TK, D)[:, :1]
+        v = V_stack.reshape(U, n_q, TK, D)[:, :1]
+        if not Q_stack.is_cuda:
+            q, k, v = (t.to(torch.bfloat16).contiguous() for t in (q, k, v))
+            o = api.prefill_host(q, k, v, start_pos=s0, causal=causal, out_dtype=self.out_dtype, device=dev)
+            return o.view(N, BR, D)
+        q, k, v = (t.to(device=dev, dtype=torch.bfloat16).contiguous() for t in (q, k, v))
+        o = api.prefill(q, k, v, start_pos=s0, causal=causal, out_dtype=self.out_dtype).view(N, BR, D)
         return o if home == o.device else o.to(home)
 
     def run_one(self, Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,

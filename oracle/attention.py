@@ -128,9 +128,11 @@ def decode_ref(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
 
 def prefill_rows_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, b: int, h: int,
                      rows: Sequence[int], start_pos: int = 0, causal: bool = True,
-                     scale: float | None = None) -> torch.Tensor:
+                     scale: float | None = None, positions: Sequence[int] | None = None) -> torch.Tensor:
     """fp32 attention for selected query rows of one (batch, query head): used
-    to check large problems on a sample of rows. Returns [len(rows), D]."""
+    to check large problems on a sample of rows. Row r sits at absolute
+    position start_pos + r, or positions[i] for the i-th row when given (so q
+    may hold only the sampled rows). Returns [len(rows), D]."""
     Hq, D = q.shape[1], q.shape[3]
     hk = h // (Hq // k.shape[1])
     sc = (1.0 / math.sqrt(D)) if scale is None else scale
@@ -139,7 +141,10 @@ def prefill_rows_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, b: int, 
     vf = v[b, hk].float()
     s = (qr @ kf.T) * sc
     if causal:
-        pos = torch.as_tensor(list(rows))[:, None] + start_pos
+        if positions is not None:
+            pos = torch.as_tensor(list(positions))[:, None]
+        else:
+            pos = torch.as_tensor(list(rows))[:, None] + start_pos
         s = s.masked_fill(torch.arange(kf.shape[0])[None, :] > pos, NEG_INF)
     dead = torch.isneginf(s).all(dim=-1, keepdim=True)
     p = torch.softmax(s.masked_fill(dead, 0.0), dim=-1).masked_fill(dead, 0.0)

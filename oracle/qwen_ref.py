@@ -111,3 +111,49 @@ def attn_forward(x: torch.Tensor, layer: QwenAttnLayer, cfg: QwenAttnConfig, cos
     out = torch.matmul(attn, vt).transpose(1, 2).contiguous()
     out = (out * torch.sigmoid(q_gate)).view(B, T, Hq * Dh)
     return (out if pre_proj else F.linear(out, layer.wo)), (k, v)
+
+
+# Golden cases run through the reference's own attn_forward by
+# tests/golden/make_golden.py (qwen_attn.npz). The head geometry is Qwen3.6's
+# (16 / 2 heads, head_dim 256, rope_dim 64, theta 1e7); d_model is 256 to keep
+# the fixture small (it only sizes the projections around the attention).
+# Weights and inputs are regenerated from these seeds at test time, and their
+# SHA-256 fingerprints are stored next to the outputs.
+QWEN_GOLDEN_CASES = {
+    # tag: (dtype, batch, prefill tokens, decode steps, weight seed, input seed)
+    "f32": (torch.float32, 2, 300, 4, 31, 32),
+    "bf16": (torch.bfloat16, 1, 40, 2, 33, 34),
+}
+QWEN_GOLDEN_MAX_POS = 1024
+
+
+def golden_config() -> QwenAttnConfig:
+    return QwenAttnConfig(d_model=256)
+
+
+def golden_case(tag: str):
+    """(cfg, layer, prefill x, [decode x per step]) for one golden case."""
+    dtype, B, T, steps, wseed, xseed = QWEN_GOLDEN_CASES[tag]
+    cfg = golden_config()
+    layer = make_layer(cfg, seed=wseed, dtype=dtype)
+    g = torch.Generator().manual_seed(xseed)
+    x = torch.randn(B, T, cfg.d_model, generator=g).to(dtype)
+    xs = [torch.randn(B, 1, cfg.d_model, generator=g).to(dtype) for _ in range(steps)]
+    return cfg, layer, x, xs
+
+
+def fingerprint(*tensors: torch.Tensor) -> str:
+    """SHA-256 over the raw bytes of the tensors (bf16 as its bit pattern)."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for t in tensors:
+        t = t.detach().contiguous()
+        if t.dtype == torch.bfloat16:
+            t = t.view(torch.int16)
+        h.update(t.numpy().tobytes())
+    return h.hexdigest()
+
+
+def layer_tensors(layer: QwenAttnLayer) -> list:
+    return [layer.attn_norm, layer.wq, layer.wk, layer.wv, layer.wo, layer.q_norm, layer.k_norm]

@@ -5,8 +5,9 @@ Run once where the reference checkout is available:
     python tests/golden/make_golden.py --reference /path/to/BojanFaletic-NPU
 
 It imports the reference's own code — npu/fa_ref.py (flash_attention_ref,
-_torch_causal_attention) and smollm.py (SmolLM) — runs it on seeded inputs,
-and stores inputs and outputs in tests/golden/*.npz. The tests then check the
+_torch_causal_attention), smollm.py (SmolLM) and qwen/forward.py
+(attn_forward, AttnLayer, with qwen/model.py's Config) — runs it on seeded
+inputs, and stores inputs and outputs in tests/golden/*.npz. The tests then check the
 oracle in oracle/ against these files; nothing at test time reads the
 reference checkout.
 """
@@ -92,20 +93,73 @@ def smollm_cases(smollm, Config, make_state_dict) -> dict:
     return out
 
 
+def qwen_cases(qf, qm) -> dict:
+    """The reference's gated attention (qwen/forward.py:133-239) on seeded
+    random weights: a prefill from position 0, then single-token decode steps
+    that feed the returned cache back in, exactly as the reference's forward
+    loop does. The weights and inputs come from oracle.qwen_ref.golden_case
+    (seeded, regenerated at test time); their SHA-256 fingerprints are stored.
+    Stored outputs: every step's block output, and sampled rows of the final
+    (k, v) cache of expanded heads."""
+    from oracle import qwen_ref as R
+
+    out = {}
+    for tag in R.QWEN_GOLDEN_CASES:
+        cfg, layer, x, xs = R.golden_case(tag)
+        dtype = x.dtype
+        ref_cfg = qm.Config(arch="qwen35moe", n_layer=1, n_ctx_train=R.QWEN_GOLDEN_MAX_POS, d_model=cfg.d_model,
+                            n_head=cfg.n_head, n_head_kv=cfg.n_head_kv, head_dim=cfg.head_dim,
+                            rms_eps=cfg.rms_eps, rope_theta=cfg.rope_theta, rope_dim=cfg.rope_dim, n_expert=1,
+                            n_expert_used=1, d_expert_ff=1, vocab_size=1, bos_id=0, eos_id=0, pad_id=None,
+                            is_attention=[True])
+        ref_layer = qf.AttnLayer(i=0, attn_norm=layer.attn_norm, post_norm=torch.ones_like(layer.attn_norm),
+                                 wq=layer.wq, wk=layer.wk, wv=layer.wv, wo=layer.wo, q_norm=layer.q_norm,
+                                 k_norm=layer.k_norm)
+        cos, sin = qf.build_partial_rope_cache(cfg.rope_dim, R.QWEN_GOLDEN_MAX_POS, cfg.rope_theta, dtype=dtype)
+        keep = bf16_bits if dtype == torch.bfloat16 else (lambda t: t.numpy().copy())
+        with torch.no_grad():
+            y, cache = qf.attn_forward(x, ref_layer, ref_cfg, cos, sin, None, 0)
+            out[f"qwen_{tag}_prefill_out"] = keep(y)
+            pos = x.shape[1]
+            for i, xi in enumerate(xs):
+                y, cache = qf.attn_forward(xi, ref_layer, ref_cfg, cos, sin, cache, pos)
+                out[f"qwen_{tag}_decode{i}_out"] = keep(y)
+                pos += 1
+        rows = sorted({0, 1, 127, 128, x.shape[1] - 1, x.shape[1], pos - 1} & set(range(pos)))
+        out[f"qwen_{tag}_cache_rows"] = np.array(rows, dtype=np.int64)
+        out[f"qwen_{tag}_cache_k"] = keep(cache[0][:, rows].contiguous())
+        out[f"qwen_{tag}_cache_v"] = keep(cache[1][:, rows].contiguous())
+        out[f"qwen_{tag}_cos_rows"] = keep(cos[rows].contiguous())
+        out[f"qwen_{tag}_sin_rows"] = keep(sin[rows].contiguous())
+        out[f"qwen_{tag}_weights_sha256"] = np.array(R.fingerprint(*R.layer_tensors(layer)))
+        out[f"qwen_{tag}_inputs_sha256"] = np.array(R.fingerprint(x, *xs))
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", choices=["fa_ref", "smollm", "qwen"], action="append",
+                    help="write only these fixtures (default: all)")
     a = ap.parse_args()
+    want = set(a.only or ["fa_ref", "smollm", "qwen"])
     ref = Path(a.reference)
     sys.path.insert(0, str(ref))  # smollm.py imports npu.profiler
     sys.path.insert(0, str(REPO))
     torch.set_num_threads(max(1, torch.get_num_threads()))
-    fa_ref = load_module("ref_fa_ref", ref / "npu" / "fa_ref.py")
-    np.savez_compressed(HERE / "fa_ref_cases.npz", **fa_ref_cases(fa_ref))
-    smollm = load_module("ref_smollm", ref / "smollm.py")
-    from oracle.smollm_ref import Config, make_state_dict
+    if "fa_ref" in want:
+        fa_ref = load_module("ref_fa_ref", ref / "npu" / "fa_ref.py")
+        np.savez_compressed(HERE / "fa_ref_cases.npz", **fa_ref_cases(fa_ref))
+    if "smollm" in want:
+        smollm = load_module("ref_smollm", ref / "smollm.py")
+        from oracle.smollm_ref import Config, make_state_dict
 
-    np.savez_compressed(HERE / "smollm_logits.npz", **smollm_cases(smollm, Config, make_state_dict))
+        np.savez_compressed(HERE / "smollm_logits.npz", **smollm_cases(smollm, Config, make_state_dict))
+    if "qwen" in want:
+        import qwen.forward as qf  # qwen/forward.py imports qwen.model (gguf) by package name
+        import qwen.model as qm
+
+        np.savez_compressed(HERE / "qwen_attn.npz", **qwen_cases(qf, qm))
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

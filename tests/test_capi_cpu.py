@@ -253,3 +253,30 @@ def test_prefill_host_python_argument_checks():
     if not torch.cuda.is_available():
         with pytest.raises(RuntimeError):
             api.prefill_host(q, k, k)  # no device: no CPU path
+
+
+def test_noalloc_scratch_constant_and_checks_without_gpu():
+    """b2a_decode_noalloc: the Python mirror of B2A_NOALLOC_SCRATCH_BYTES
+    matches the header, and a problem that cannot fit the fixed scratch is
+    rejected before any CUDA call (FAKE pointers are never dereferenced)."""
+    text = (ROOT / "include" / "b2attn.h").read_text()
+    m = re.search(r"#define\s+B2A_NOALLOC_SCRATCH_BYTES\s+\((\d+)u\s*\*\s*(\d+)u\s*\*\s*(\d+)u\)", text)
+    assert m, "B2A_NOALLOC_SCRATCH_BYTES not found in b2attn.h"
+    assert int(m[1]) * int(m[2]) * int(m[3]) == _lib.B2A_NOALLOC_SCRATCH_BYTES
+    lib = _lib.load()
+
+    def call(B, Hq, Hkv, L, D, split):
+        return lib.b2a_decode_noalloc(FAKE, FAKE, FAKE, FAKE, FAKE, B, Hq, Hkv, L, D,
+                                      _lib.ll2(Hq * D, D), _lib.ll3(Hkv * L * D, L * D, D),
+                                      _lib.ll3(Hkv * L * D, L * D, D), _lib.ll2(Hq * D, D), 0.1, split, 1, None)
+
+    # an explicit split whose partials exceed the scratch
+    assert lib.b2a_decode_workspace_bytes(16, 32, 8, 256, 4096, 64) > _lib.B2A_NOALLOC_SCRATCH_BYTES
+    assert call(16, 32, 8, 4096, 256, 64) == _lib.B2A_ERR_WORKSPACE
+    # default split: even one split per sequence needs B*Hq*D*4 bytes > 16 MiB
+    assert lib.b2a_decode_workspace_bytes(128, 128, 8, 256, 64, 64) > _lib.B2A_NOALLOC_SCRATCH_BYTES
+    assert call(128, 128, 8, 64, 256, 0) == _lib.B2A_ERR_WORKSPACE
+    if not torch.cuda.is_available():
+        # config-4 geometry fits once the split is lengthened; without a GPU the
+        # call then stops at the device lookup
+        assert call(128, 32, 4, 32768, 128, 0) in (_lib.B2A_ERR_CUDA, _lib.B2A_ERR_DEVICE)

@@ -89,3 +89,29 @@ def test_decode_length_beyond_cache_is_reported(cuda_dev):
     assert api.device_error(clear=True) == _lib.B2A_ERR_DEVICE_BAD_LEN
     ref = A.decode_ref(q, kc, vc, [128])
     assert (out.cpu() - ref).abs().max().item() <= TOL
+
+
+def test_config4_all_128_sequences(cuda_dev):
+    """Config 4 at its benchmarked size: 128 sequences, lengths ~ U[1024,
+    32768] (seed 0 as in the bench), 32 query / 4 KV heads, D=128, 32k-key
+    caches, the default split length. Every output is finite; the shortest,
+    the longest and six more sequences are checked against the oracle."""
+    from npu_b200 import api
+
+    B, Hq, Hkv, D, Lmax = 128, 32, 4, 128, 32768
+    lens = torch.randint(1024, Lmax + 1, (B,), generator=torch.Generator().manual_seed(0))
+    g = torch.Generator(device=cuda_dev).manual_seed(44)
+    q = torch.randn(B, Hq, D, generator=g, device=cuda_dev, dtype=torch.bfloat16)
+    kc = torch.randn(B, Hkv, Lmax, D, generator=g, device=cuda_dev, dtype=torch.bfloat16)
+    vc = torch.randn(B, Hkv, Lmax, D, generator=g, device=cuda_dev, dtype=torch.bfloat16)
+    sl = lens.to(torch.int32).to(cuda_dev)
+    out = api.decode(q, kc, vc, sl, scale=1 / math.sqrt(D), out_dtype=torch.bfloat16)
+    assert api.device_error() == 0
+    assert torch.isfinite(out.float()).all()
+    pick = sorted({int(lens.argmin()), int(lens.argmax()), 0, 1, 37, 64, 100, 127})
+    for b in pick:
+        L = int(lens[b])
+        ref = A.decode_ref(q[b:b + 1].cpu(), kc[b:b + 1, :, :L].cpu(), vc[b:b + 1, :, :L].cpu(), [L],
+                           scale=1 / math.sqrt(D))
+        err = (out[b:b + 1].float().cpu() - ref).abs().max().item()
+        assert err <= TOL, (b, L, err)

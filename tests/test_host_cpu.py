@@ -24,3 +24,46 @@ def test_qwen_drop_in_weight_copies_follow_the_layer_object():
     # Weights already on the target device and dtype are used as they are.
     same = R.make_layer(rc, seed=2, dtype=torch.bfloat16)
     assert m._layer_on_device(same, torch.device("cpu"), torch.bfloat16)["wo"] is same.wo
+
+
+def _reference_stacks(B, Hq, T, Tk, BR, D, start_pos, seed=0):
+    """Q/K/V stacks and start rows exactly as smollm.py:147-161 builds them."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, Hq, T, D, generator=g)
+    k = torch.randn(B, Hq, Tk, D, generator=g)
+    v = torch.randn(B, Hq, Tk, D, generator=g)
+    n_q = -(-T // BR)
+    q = torch.cat([q, q.new_zeros(B, Hq, n_q * BR - T, D)], dim=2)
+    N = B * Hq * n_q
+    q_stack = q.view(B, Hq, n_q, BR, D).reshape(N, BR, D).contiguous()
+    k_stack = k.unsqueeze(2).expand(B, Hq, n_q, Tk, D).reshape(N, Tk, D).contiguous()
+    v_stack = v.unsqueeze(2).expand(B, Hq, n_q, Tk, D).reshape(N, Tk, D).contiguous()
+    rows = [i * BR + start_pos for _ in range(B * Hq) for i in range(n_q)]
+    return q_stack, k_stack, v_stack, rows, n_q
+
+
+def test_run_batch_recognises_the_reference_block_layout():
+    """NpuAttention finds the (batch, head) units of the reference caller's
+    stacks (n_q blocks per unit, identical K/V within a unit) and refuses
+    anything else, which then runs block by block."""
+    from npu_b200 import NpuAttention
+
+    attn = NpuAttention(BR=32, BC=32, D=64, n_cores=4)  # smollm.py:318
+    q, k, v, rows, n_q = _reference_stacks(2, 3, 100, 128, 32, 64, start_pos=0)
+    assert n_q == 4 and attn._units_of_blocks(k, v, rows) == 4
+    q, k, v, rows, n_q = _reference_stacks(1, 2, 64, 96, 32, 64, start_pos=32, seed=1)  # chunked prefill
+    assert attn._units_of_blocks(k, v, rows) == 2
+    # one K element changed inside a unit
+    k2 = k.clone()
+    k2[1, 5, 3] += 1.0
+    assert attn._units_of_blocks(k2, v, rows) == 1
+    # a V difference too
+    v2 = v.clone()
+    v2[3, 0, 0] -= 1.0
+    assert attn._units_of_blocks(k, v2, rows) == 1
+    # start rows that do not follow i * BR + s0, or a dummy block
+    assert attn._units_of_blocks(k, v, [0, 32, 0, 33]) == 1
+    assert attn._units_of_blocks(k, v, [0, 32, 0, -1_000_000]) == 1
+    # single blocks (decode through run_batch) stay on the per-block path
+    assert attn._units_of_blocks(k[:1], v[:1], [7]) == 1
+    assert attn._units_of_blocks(k, v, [5, 5, 5, 5]) == 1

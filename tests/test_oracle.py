@@ -135,3 +135,51 @@ def test_smollm_hook_routes_attention_through_run_batch():
     assert FakeAttn.calls == cfg.n_layers
     assert torch.allclose(hooked, base, atol=5e-2)
     assert int(hooked[0, -1].argmax()) == int(base[0, -1].argmax())
+
+
+def _qwen_golden():
+    from conftest import GOLDEN
+    return dict(np.load(GOLDEN / "qwen_attn.npz"))
+
+
+def _as_torch(a: np.ndarray, dtype: torch.dtype) -> torch.Tensor:
+    return from_bits(a) if dtype == torch.bfloat16 else torch.from_numpy(a.copy())
+
+
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+def test_qwen_oracle_matches_reference_attn_forward(tag):
+    """oracle/qwen_ref.py against outputs of the reference's own
+    qwen/forward.py attn_forward (tests/golden/make_golden.py): a prefill from
+    position 0 and single-token decode steps through the returned cache."""
+    from oracle import qwen_ref as R
+
+    g = _qwen_golden()
+    cfg, layer, x, xs = R.golden_case(tag)
+    dtype = x.dtype
+    # the seeded weights and inputs are the ones the reference ran on
+    assert R.fingerprint(*R.layer_tensors(layer)) == str(g[f"qwen_{tag}_weights_sha256"])
+    assert R.fingerprint(x, *xs) == str(g[f"qwen_{tag}_inputs_sha256"])
+    cos, sin = R.partial_rope_tables(cfg.rope_dim, R.QWEN_GOLDEN_MAX_POS, cfg.rope_theta, dtype)
+    rows = g[f"qwen_{tag}_cache_rows"].tolist()
+    assert torch.equal(cos[rows], _as_torch(g[f"qwen_{tag}_cos_rows"], dtype))
+    assert torch.equal(sin[rows], _as_torch(g[f"qwen_{tag}_sin_rows"], dtype))
+    # fp32: the restatement reorders nothing that matters beyond rounding;
+    # bf16: one bf16 step of the largest output
+    tol = 1e-5 if dtype == torch.float32 else 1.0 / 128
+
+    def close(got, key):
+        want = _as_torch(g[key], dtype).float()
+        scale = max(1.0, want.abs().max().item())
+        assert (got.float() - want).abs().max().item() <= tol * scale, key
+
+    with torch.no_grad():
+        y, cache = R.attn_forward(x, layer, cfg, cos, sin, None, 0)
+        close(y, f"qwen_{tag}_prefill_out")
+        pos = x.shape[1]
+        for i, xi in enumerate(xs):
+            y, cache = R.attn_forward(xi, layer, cfg, cos, sin, cache, pos)
+            close(y, f"qwen_{tag}_decode{i}_out")
+            pos += 1
+    assert cache[0].shape[1] == pos
+    close(cache[0][:, rows], f"qwen_{tag}_cache_k")
+    close(cache[1][:, rows], f"qwen_{tag}_cache_v")

@@ -323,3 +323,31 @@ def test_config5_geometry_sampled_rows(cuda_dev):
         ref = A.prefill_rows_ref(qc, kc, vc, 0, h, rows, scale=1 / 16)
         assert (out[0, h, rows].cpu() - ref).abs().max().item() <= TOL
     assert torch.isfinite(out).all()
+
+
+def test_config5_full_length_sampled_rows(cuda_dev):
+    """Config 5 at its benchmarked length, T=131072 (16 query / 2 KV heads,
+    D=256, scale 1/16, one sequence): the first row, the middle, the last row
+    and both sides of each of the last four 128-row tile boundaries, i.e. the
+    end of a 1024-block causal key walk, against the oracle."""
+    from npu_b200 import api
+
+    T = 131072
+    g = torch.Generator(device=cuda_dev).manual_seed(55)
+    q = torch.randn(1, 16, T, 256, generator=g, device=cuda_dev, dtype=torch.bfloat16)
+    k = torch.randn(1, 2, T, 256, generator=g, device=cuda_dev, dtype=torch.bfloat16)
+    v = torch.randn(1, 2, T, 256, generator=g, device=cuda_dev, dtype=torch.bfloat16)
+    out = api.prefill(q, k, v, scale=1 / 16, out_dtype=torch.bfloat16)
+    assert api.device_error() == 0
+    rows = [0, 1, 65535, 65536]
+    for j in range(1, 5):
+        rows += [T - 128 * j - 1, T - 128 * j]
+    rows += [T - 1]
+    rows = sorted(set(rows))
+    kc, vc = k.cpu(), v.cpu()
+    qr = q[:, :, rows].cpu()  # only the sampled rows leave the device
+    for h in (0, 7, 8, 15):
+        ref = A.prefill_rows_ref(qr, kc, vc, 0, h, range(len(rows)), scale=1 / 16, positions=rows)
+        err = (out[0, h, rows].float().cpu() - ref).abs().max().item()
+        assert err <= TOL, (h, err)
+    assert not torch.isnan(out).any()

@@ -1,10 +1,14 @@
 """Qwen3.5/3.6 gated attention (qwen/forward.py:133-239) on the B200 path —
 fused per-head Q/K RMSNorm + partial RoPE + KV append, attention with the
-sigmoid gate fused into its output stores — against the reference's CPU
-attention restated in oracle/qwen_ref.py (seeded random weights; the GGUF
-checkpoint is not available offline)."""
+sigmoid gate fused into its output stores — against outputs of the
+reference's own attn_forward (tests/golden/qwen_attn.npz) and against its CPU
+restatement in oracle/qwen_ref.py (seeded random weights; the GGUF checkpoint
+is not available offline)."""
+import numpy as np
 import pytest
 import torch
+
+from conftest import GOLDEN, from_bits
 
 from oracle import qwen_ref as R
 
@@ -115,3 +119,41 @@ def test_attn_forward_drop_in_matches_reference_signature(cuda_dev, dtype):
     for mine, theirs in zip(cache, ref_cache):
         assert mine.shape == theirs.shape
         assert (mine.float().cpu() - theirs.float()).abs().max().item() < 5e-2 * max(1.0, theirs.float().abs().max())
+
+
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+def test_attn_forward_drop_in_matches_reference_golden(cuda_dev, tag):
+    """The drop-in attn_forward against the outputs the reference's own
+    qwen/forward.py attn_forward produced on the same seeded weights and
+    inputs: the prefill from position 0 (300 tokens, batch 2, fp32; 40 tokens
+    in bf16), then the single-token decode steps through the returned cache."""
+    from npu_b200.qwen_attention import attn_forward
+
+    g = dict(np.load(GOLDEN / "qwen_attn.npz"))
+    cfg, layer, x, xs = R.golden_case(tag)
+    assert R.fingerprint(*R.layer_tensors(layer)) == str(g[f"qwen_{tag}_weights_sha256"])
+    assert R.fingerprint(x, *xs) == str(g[f"qwen_{tag}_inputs_sha256"])
+    dtype = x.dtype
+    cos, sin = R.partial_rope_tables(cfg.rope_dim, R.QWEN_GOLDEN_MAX_POS, cfg.rope_theta, dtype)
+
+    def check(got, key):
+        a = g[key]
+        want = (from_bits(a) if dtype == torch.bfloat16 else torch.from_numpy(a.copy())).float()
+        scale = max(1.0, want.abs().max().item())
+        err = (got.float().cpu() - want).abs().max().item()
+        assert err <= TOL * scale, (key, err)
+
+    out, cache = attn_forward(x, layer, cfg, cos, sin, None, 0, device=cuda_dev)
+    assert out.dtype == dtype and out.device == x.device
+    check(out, f"qwen_{tag}_prefill_out")
+    pos = x.shape[1]
+    for i, xi in enumerate(xs):
+        out, cache = attn_forward(xi, layer, cfg, cos, sin, cache, pos, device=cuda_dev)
+        check(out, f"qwen_{tag}_decode{i}_out")
+        pos += 1
+    rows = g[f"qwen_{tag}_cache_rows"].tolist()
+    for j, key in enumerate(("cache_k", "cache_v")):
+        a = g[f"qwen_{tag}_{key}"]
+        want = (from_bits(a) if dtype == torch.bfloat16 else torch.from_numpy(a.copy())).float()
+        got = cache[j][:, rows].float().cpu()  # bf16 cache: one rounding of the reference's values
+        assert (got - want).abs().max().item() <= 1e-2 * max(1.0, want.abs().max().item()), key

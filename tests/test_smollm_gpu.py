@@ -78,3 +78,73 @@ def test_decode_attention_through_run_batch(cuda_dev, cpu_model):
             layer.npu_decode_attention = False
     assert int(logits[0, -1].argmax()) == int(ref_logits[0, -1].argmax())
     assert (logits[0, -1] - ref_logits[0, -1]).abs().max().item() < 0.25
+
+
+def test_config2_reference_attention_object_on_host_model(cuda_dev, cpu_model):
+    """The reference's own deployment at config 2: the 30-layer model stays on
+    the CPU and every layer's attention goes through the object smollm.py:318
+    constructs, NpuAttention(BR=32, BC=32, D=64, n_cores=4), at T=1024. The
+    caller duplicates K/V per 32-row block (smollm.py:157-161); run_batch must
+    recognise that layout and run each (batch, head) once. Top-1 must match
+    the CPU attention path."""
+    from npu_b200 import NpuAttention
+
+    ids = _ids(1024)
+    ref_logits, _ = cpu_model.forward(ids)
+    attn = NpuAttention(BR=32, BC=32, D=64, n_cores=4)
+    units = []
+    orig = attn._run_units
+
+    def counting(*a, **kw):
+        units.append(a[4])  # n_q
+        return orig(*a, **kw)
+
+    attn._run_units = counting
+    for layer in cpu_model.layers:
+        layer.npu = {"attention": attn}
+    try:
+        logits, _ = cpu_model.forward(ids)
+    finally:
+        for layer in cpu_model.layers:
+            layer.npu = None
+    assert units == [1024 // 32] * 30  # every layer took the one-prefill-per-unit path
+    last, ref_last = logits[0, -1], ref_logits[0, -1]
+    assert int(last.argmax()) == int(ref_last.argmax())
+    assert (last - ref_last).abs().max().item() < 0.25
+
+
+def test_run_batch_units_match_blockwise_and_oracle(cuda_dev):
+    """The one-prefill-per-unit path and the block-by-block path give the
+    same rows (within the parity tolerance of the oracle) on host and device
+    stacks, for BR=32 with a ragged last block and a chunked start."""
+    from npu_b200 import NpuAttention
+    from oracle import attention as A
+
+    attn = NpuAttention(BR=32, BC=32, D=64, n_cores=4)
+    g = torch.Generator().manual_seed(3)
+    B, Hq, T, Tk, BR, D, sp = 1, 3, 90, 128, 32, 64, 38
+    q = torch.randn(B, Hq, T, D, generator=g)
+    k = torch.randn(B, Hq, Tk, D, generator=g)
+    v = torch.randn(B, Hq, Tk, D, generator=g)
+    n_q = -(-T // BR)
+    q = torch.cat([q, q.new_zeros(B, Hq, n_q * BR - T, D)], dim=2)
+    N = B * Hq * n_q
+    Q = q.view(B, Hq, n_q, BR, D).reshape(N, BR, D).contiguous()
+    K = k.unsqueeze(2).expand(B, Hq, n_q, Tk, D).reshape(N, Tk, D).contiguous()
+    V = v.unsqueeze(2).expand(B, Hq, n_q, Tk, D).reshape(N, Tk, D).contiguous()
+    rows = [i * BR + sp for _ in range(B * Hq) for i in range(n_q)]
+    assert attn._units_of_blocks(K, V, rows) == n_q
+    ref = A.run_batch_ref(Q.bfloat16(), K.bfloat16(), V.bfloat16(), rows)
+    host = attn.run_batch(Q, K, V, rows)
+    dev = attn.run_batch(Q.to(cuda_dev), K.to(cuda_dev), V.to(cuda_dev), rows)
+    assert host.device.type == "cpu" and dev.device == torch.device(cuda_dev)
+    assert host.shape == dev.shape == (N, BR, D) and host.dtype == dev.dtype == torch.bfloat16
+    assert torch.equal(host, dev.cpu())
+    assert (host.float() - ref).abs().max().item() <= 2e-2
+    # Break the layout (one K element) -> block-by-block path, same values.
+    K2 = K.clone()
+    K2[1, 0, 0] += 0.0078125
+    assert attn._units_of_blocks(K2, V, rows) == 1
+    blockwise = attn.run_batch(Q, K2, V, rows)
+    ref2 = A.run_batch_ref(Q.bfloat16(), K2.bfloat16(), V.bfloat16(), rows)
+    assert (blockwise.float() - ref2).abs().max().item() <= 2e-2
