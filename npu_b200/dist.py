@@ -74,7 +74,15 @@ class ContextParallelPrefill:
     [B, Hkv, 2c, D]: the rows of its two chunks (zigzag_chunks) back to back.
     `run` all-gathers K and V into [B, Hkv, T, D] and returns this rank's
     output rows [B, Hq, 2c, D]. `attn_fn(q, k, v, start_pos)` is the
-    attention kernel (npu_b200.api.prefill by default).
+    attention kernel (npu_b200.api.prefill by default, which then writes both
+    chunks' rows straight into `out`).
+
+    The gather runs in two halves. Rank g's first chunk is chunk g, so the
+    first chunks of all ranks are rows [0, T/2) in rank order; its second
+    chunk is chunk 2G-1-g, so the second chunks are rows [T/2, T) in reverse
+    rank order. A rank's first chunk needs keys from the first half only: its
+    attention runs while the second half is still being gathered, and the
+    second chunk (which needs every key before it) runs after it.
     """
 
     T: int
@@ -86,34 +94,68 @@ class ContextParallelPrefill:
     def __post_init__(self):
         self.chunks = zigzag_chunks(self.T, self.world, self.rank)
         self.c = self.T // (2 * self.world)
+        self.launches_per_run = 2
 
-    def gather_kv(self, k_local: torch.Tensor, v_local: torch.Tensor):
+    def _gather_half(self, k_part: torch.Tensor, v_part: torch.Tensor, async_op: bool):
+        """All ranks' [B, H, c, D] K and V parts -> [world, 2, B, H, c, D] in
+        rank order (one collective for K and V together)."""
         import torch.distributed as dist
 
+        send = torch.stack([k_part, v_part])
+        flat = torch.empty((self.world * 2,) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
+        work = dist.all_gather_into_tensor(flat, send, group=self.group, async_op=async_op)
+        return flat.view((self.world,) + tuple(send.shape)), work
+
+    def _place(self, full: torch.Tensor, recv: torch.Tensor, second: bool) -> None:
+        """Copy one gathered half into its rows of full [2, B, H, T, D]: rank
+        g's first chunk is chunk g, its second chunk is chunk 2G-1-g."""
+        _, B, H, T, D = full.shape
+        w, c = self.world, self.c
+        src = recv.permute(1, 2, 3, 0, 4, 5)  # [2, B, H, world, c, D]
+        if second:
+            src = src.flip(3)
+        half = full[:, :, :, w * c:] if second else full[:, :, :, :w * c]
+        half.view(2, B, H, w, c, D).copy_(src)
+
+    def gather_kv(self, k_local: torch.Tensor, v_local: torch.Tensor):
+        """Blocking gather of the whole sequence's K and V [B, H, T, D]."""
         B, H, two_c, D = k_local.shape
         assert two_c == 2 * self.c
-        kv = torch.stack([k_local, v_local])  # [2, B, H, 2c, D]
-        flat = torch.empty((self.world * 2,) + tuple(kv.shape[1:]), dtype=kv.dtype, device=kv.device)
-        dist.all_gather_into_tensor(flat, kv.contiguous(), group=self.group)
-        buf = flat.view((self.world,) + tuple(kv.shape))
-        full = torch.empty((2, B, H, self.T, D), dtype=kv.dtype, device=kv.device)
-        c, n = self.c, 2 * self.world
-        for r in range(self.world):
-            for slot, chunk in enumerate((r, n - 1 - r)):
-                full[:, :, :, chunk * c:(chunk + 1) * c] = buf[r, :, :, :, slot * c:(slot + 1) * c]
+        c = self.c
+        full = torch.empty((2, B, H, self.T, D), dtype=k_local.dtype, device=k_local.device)
+        r1, _ = self._gather_half(k_local[:, :, :c], v_local[:, :, :c], async_op=False)
+        r2, _ = self._gather_half(k_local[:, :, c:], v_local[:, :, c:], async_op=False)
+        self._place(full, r1, second=False)
+        self._place(full, r2, second=True)
         return full[0], full[1]
 
-    def run(self, q_local: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor, **kw) -> torch.Tensor:
-        attn = self.attn_fn
-        if attn is None:
+    def run(self, q_local: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,
+            out: Optional[torch.Tensor] = None, **kw) -> torch.Tensor:
+        B, H, two_c, D = k_local.shape
+        assert two_c == 2 * self.c
+        c = self.c
+        full = torch.empty((2, B, H, self.T, D), dtype=k_local.dtype, device=k_local.device)
+        r1, w1 = self._gather_half(k_local[:, :, :c], v_local[:, :, :c], async_op=True)
+        r2, w2 = self._gather_half(k_local[:, :, c:], v_local[:, :, c:], async_op=True)
+        if self.attn_fn is None:
             from .api import prefill
 
-            def attn(q, k, v, start_pos, **kw2):
-                return prefill(q, k, v, start_pos=start_pos, causal=True, **kw2)
+            if out is None:
+                out = torch.empty(q_local.shape, dtype=kw.get("out_dtype", torch.float32), device=q_local.device)
 
-        k_full, v_full = self.gather_kv(k_local, v_local)
+            def attend(slot, k, v, start):
+                return prefill(q_local[:, :, slot * c:(slot + 1) * c], k, v, start_pos=start, causal=True,
+                               out=out[:, :, slot * c:(slot + 1) * c], **kw)
+        else:
+            def attend(slot, k, v, start):
+                return self.attn_fn(q_local[:, :, slot * c:(slot + 1) * c], k, v, start, **kw)
+
         outs = []
-        for slot, (r0, r1) in enumerate(self.chunks):
-            qs = q_local[:, :, slot * self.c:(slot + 1) * self.c]
-            outs.append(attn(qs, k_full[:, :, :r1], v_full[:, :, :r1], r0, **kw))
+        for slot, (work, recv) in enumerate(((w1, r1), (w2, r2))):
+            work.wait()  # NCCL: the current stream waits; the host does not
+            self._place(full, recv, second=slot == 1)
+            r0, r1_ = self.chunks[slot]
+            outs.append(attend(slot, full[0, :, :, :r1_], full[1, :, :, :r1_], r0))
+        if self.attn_fn is None:
+            return out
         return torch.cat(outs, dim=2)

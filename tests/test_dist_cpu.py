@@ -78,7 +78,7 @@ def _cp_worker(rank, world, port, T, result):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4])
 def test_context_parallel_prefill_gloo(world):
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
