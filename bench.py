@@ -503,6 +503,19 @@ def run_config1(a, dist: Dist, dev) -> dict:
     f = prefill_flops(1, 9, 64, 128)
     reps = 50 * a.steps
     tot, per = timed(lambda: api.prefill(q, k, v, scale=0.125, out=o), reps, max(a.warmup, 10), dist)
+    # The same launches replayed from a CUDA graph (no host work between
+    # them): the kernel's own time per launch.
+    n_graph = 50
+    for _ in range(3):
+        api.prefill(q, k, v, scale=0.125, out=o)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(n_graph):
+            api.prefill(q, k, v, scale=0.125, out=o)
+    tot_g, _ = timed(graph.replay, a.steps, a.warmup, dist)
+    per_graph = tot_g / (a.steps * n_graph)
+    del graph
     qp, kp, vp = qh.pin_memory(), kh.pin_memory(), vh.pin_memory()
     op = torch.empty(1, 9, 128, 64, pin_memory=True)
 
@@ -513,8 +526,10 @@ def run_config1(a, dist: Dist, dev) -> dict:
     line = {"workload": "config1 SmolLM2 one-layer prefill attention, B=1, T=128, 9/3 heads, D=64",
             "parallelism": "replicas only (too small to shard)", "flops": f,
             "device_us_per_launch": per * 1e3, "device_tflops": f / (per * 1e-3) / 1e12,
+            "graph_us_per_launch": per_graph * 1e3, "graph_tflops": f / (per_graph * 1e-3) / 1e12,
+            "note": "eager launches are bound by host-side call overhead; the graph replay shows the kernel",
             "e2e_us_per_call": tot_e / reps * 1e3, "e2e_api": "npu_b200.prefill_host (pinned host buffers)",
-            "gpu_launches": 2 * reps}
+            "gpu_launches": 2 * reps + n_graph * a.steps}
     if dist.rank == 0 and dist.world == 1 and a.cpu_baseline:
         line["cpu_baseline"] = cpu_config1(qh, kh, vh)
     return line
@@ -550,9 +565,14 @@ def run_config2(a, dist: Dist, dev) -> dict:
 
         tot, per = timed(step, a.steps, a.warmup, dist)
         logits = step()[0, -1].float().cpu()
+        cache.reset()
+        graph_step = model.capture_prefill(cache, T)
+        tot_g, per_g = timed(lambda: (cache.reset(), graph_step(ids_d)), a.steps, a.warmup, dist)
+        g_logits = graph_step(ids_d)[0, -1].float().cpu()
         fwd[name] = {"ms_per_forward": per, "tokens_per_s": T / (per * 1e-3), "top1": int(logits.argmax()),
+                     "graph_ms_per_forward": per_g, "graph_top1": int(g_logits.argmax()),
                      "gpu_launches_per_forward": 30 * 2}
-        del model, cache
+        del model, cache, graph_step
     out["forward_gpu"] = fwd
     # One layer's attention through run_batch with the reference's own
     # object and stacks (model on the host): q/k/v as layer 0 produces them.

@@ -357,6 +357,15 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// griddepcontrol.wait: block until the grid this one depends on (the previous
+// kernel in the stream, when this grid was launched with programmatic stream
+// serialization) has completed and its memory is visible; a no-op otherwise.
+// griddepcontrol.launch_dependents: this CTA no longer holds back the launch
+// of the next grid (which still waits in its own griddepcontrol.wait).
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
                : "memory");

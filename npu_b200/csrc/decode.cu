@@ -85,6 +85,12 @@ __global__ void __launch_bounds__(160)
   DecodeBars* bars = reinterpret_cast<DecodeBars*>(smem + C::OFF_BAR);
   volatile int* abort_flag = &bars->abort_flag;
 
+  // Launched as a programmatic dependent of the previous kernel in the
+  // stream: nothing that kernel may write is read before this wait.
+  grid_dep_wait();
+  // The combine kernel may launch now; it waits for this whole grid in its
+  // own grid_dep_wait, so its CTAs only take SM slots that split CTAs free.
+  grid_dep_launch();
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   int L = p.seqlens[b];
   if (L > p.Lmax || L < 0) {
@@ -286,6 +292,7 @@ __global__ void __launch_bounds__(160)
 
 // One CTA per (sequence, query head); thread d owns output column d.
 __global__ void decode_combine_kernel(const __grid_constant__ DecodeParams p, int D) {
+  grid_dep_wait();  // every split's partials are written and visible
   const int bh = blockIdx.x;
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int g = h / p.group, r = h % p.group;
@@ -327,11 +334,25 @@ static int launch_decode_t(const CUtensorMap& tk, const CUtensorMap& tv, const D
   cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM_BYTES);
   if (e != cudaSuccess) return -1;
-  dim3 grid((unsigned)p.max_splits, (unsigned)p.Hkv, (unsigned)p.B);
-  decode_split_kernel<D><<<grid, C::THREADS, C::SMEM_BYTES, st>>>(tk, tv, p);
-  if (cudaGetLastError() != cudaSuccess) return -1;
-  const int threads = D < 128 ? 64 : 128;
-  decode_combine_kernel<<<(unsigned)(p.B * p.Hq), threads, 0, st>>>(p, D);
+  // Both kernels are launched with programmatic stream serialization: each
+  // may be scheduled while the kernel before it drains, and waits for it in
+  // grid_dep_wait before reading anything (split: the previous kernel's
+  // outputs, e.g. q or a cache append; combine: the split's partials).
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)p.max_splits, (unsigned)p.Hkv, (unsigned)p.B);
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, decode_split_kernel<D>, tk, tv, p) != cudaSuccess) return -1;
+  cfg.gridDim = dim3((unsigned)(p.B * p.Hq));
+  cfg.blockDim = dim3(D < 128 ? 64 : 128);
+  cfg.dynamicSmemBytes = 0;
+  if (cudaLaunchKernelEx(&cfg, decode_combine_kernel, p, D) != cudaSuccess) return -1;
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

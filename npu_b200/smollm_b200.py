@@ -119,9 +119,12 @@ class SmolLMB200:
             o = api.decode(q_rot[:, :, 0], k_cache, v_cache, cache.end, out_dtype=h.dtype,
                            workspace=self._workspace(B, cache.max_len))
             return o.reshape(B, 1, Hq * Dh)
-        o = api.prefill(q_rot, k_cache, v_cache, start_pos_per_batch=cache.start,
-                        scale=1.0 / math.sqrt(Dh), causal=True, out_dtype=h.dtype)
-        return o.transpose(1, 2).reshape(B, T, Hq * Dh)
+        # The kernel writes O straight into the [B, T, Hq * Dh] layout the
+        # output projection reads (a strided [B, Hq, T, Dh] view of it).
+        o = torch.empty((B, T, Hq, Dh), dtype=h.dtype, device=h.device)
+        api.prefill(q_rot, k_cache, v_cache, start_pos_per_batch=cache.start, scale=1.0 / math.sqrt(Dh),
+                    causal=True, out_dtype=h.dtype, out=o.transpose(1, 2))
+        return o.view(B, T, Hq * Dh)
 
     @torch.no_grad()
     def capture_decode(self, cache: KVCache, warmup: int = 2):
@@ -144,6 +147,40 @@ class SmolLMB200:
             for _ in range(warmup):
                 self.forward(ids_buf, cache)
         torch.cuda.current_stream(self.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = self.forward(ids_buf, cache)
+        cache._pos.copy_(saved)
+
+        def step(ids: torch.Tensor) -> torch.Tensor:
+            ids_buf.copy_(ids)
+            graph.replay()
+            return out
+
+        step.graph = graph
+        return step
+
+    @torch.no_grad()
+    def capture_prefill(self, cache: KVCache, T: int, warmup: int = 2):
+        """A CUDA graph of one T-token prefill step over `cache` (every layer's
+        norms, fused QKV GEMM, rope_append, prefill attention, output
+        projection and MLP replayed as one launch), the prefill counterpart of
+        capture_decode. Returns step(ids [B, T]) -> logits [B, T, vocab] (a
+        buffer the next replay overwrites); each replay appends at the
+        cache's current positions and advances them, like forward. Warm-up and
+        capture run real steps and the positions are restored afterwards, so
+        the rows they wrote are overwritten by the next replay."""
+        B = cache.batch
+        ids_buf = torch.zeros((B, T), dtype=torch.long, device=self.device)
+        saved = cache._pos.clone()
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                cache._pos.copy_(saved)
+                self.forward(ids_buf, cache)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        cache._pos.copy_(saved)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             out = self.forward(ids_buf, cache)

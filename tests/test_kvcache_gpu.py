@@ -119,3 +119,24 @@ def test_smollm_decode_step_as_cuda_graph(cuda_dev):
         tok = ref[:, -1].argmax(-1, keepdim=True)
     assert graph_cache.lengths() == eager_cache.lengths() == [45, 45]
     assert api.device_error() == 0
+
+
+def test_smollm_prefill_step_as_cuda_graph(cuda_dev):
+    """A whole 64-token prefill step (30 layers) captured once and replayed
+    twice on a cache: each replay appends at the cache's positions like the
+    eager forward and gives the same logits."""
+    from npu_b200 import api
+    from npu_b200.smollm_b200 import SmolLMB200, SmolLMConfig
+
+    model = SmolLMB200(make_state_dict(Config(), seed=0), SmolLMConfig(), cuda_dev)
+    g = torch.Generator().manual_seed(10)
+    ids = [torch.randint(0, Config().vocab, (2, 64), generator=g).to(cuda_dev) for _ in range(2)]
+    eager_cache, graph_cache = model.new_cache(2, 256), model.new_cache(2, 256)
+    step = model.capture_prefill(graph_cache, 64)
+    assert graph_cache.lengths() == [0, 0]
+    for chunk in ids:
+        ref = model.forward(chunk, eager_cache)
+        got = step(chunk)
+        assert torch.allclose(got, ref, atol=1e-4, rtol=0)
+    assert graph_cache.lengths() == eager_cache.lengths() == [128, 128]
+    assert api.device_error() == 0
