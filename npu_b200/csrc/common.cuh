@@ -357,6 +357,36 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 
+// ---------------------------------------------------------------- cluster launch control
+// Ask the hardware to cancel the launch of a CTA of this grid that has not
+// started yet (a cluster of one) so that this CTA takes over its work: the
+// 16-byte response lands in `resp` (shared memory, 16-byte aligned) and
+// completes `bar` with 16 transaction bytes. Issued by one thread.
+__device__ __forceinline__ void clc_try_cancel(void* resp, uint64_t* bar) {
+  asm volatile(
+      "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(
+          smem_u32(resp)),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Decode a try_cancel response once its barrier has completed: blockIdx.x of
+// the cancelled CTA, or -1 when nothing was cancelled (every CTA of the grid
+// has started). After a -1 no further request may be made.
+__device__ __forceinline__ int clc_cancelled_ctaid_x(const void* resp) {
+  uint32_t cancelled, x = 0;
+  asm volatile(
+      "{\n\t.reg .b128 r;\n\t.reg .pred p;\n\t"
+      "ld.shared.b128 r, [%2];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, r;\n\t}\n"
+      : "=r"(cancelled), "+r"(x)
+      : "r"(smem_u32(resp))
+      : "memory");
+  return cancelled ? (int)x : -1;
+}
+
 // ---------------------------------------------------------------- programmatic dependent launch
 // griddepcontrol.wait: block until the grid this one depends on (the previous
 // kernel in the stream, when this grid was launched with programmatic stream

@@ -13,6 +13,44 @@ namespace b2a {
 constexpr int kOneTileMaxRows = B2A_ONE_TILE_MAX_ROWS;
 
 
+// Work item -> (query block, head, batch) and the key blocks its query tiles
+// need. The heaviest causal query blocks come first in launch order; the Hq
+// heads of one batch are adjacent so the query heads that share a KV head run
+// together and re-read K/V from L2.
+template <int NQT>
+struct PrefillItem {
+  int h, b, hk, q0, sp;
+  int n_t[NQT];  // key blocks query tile t needs; tile 0 (earlier rows) never
+                 // more than tile 1 and, under the causal mask, at most one fewer
+  int n_kv;      // n_t[NQT - 1]: the key blocks that get loaded
+};
+
+template <int NQT>
+__device__ __forceinline__ PrefillItem<NQT> prefill_item(const PrefillParams& p, int lin) {
+  constexpr int BM = 128, BN = 128;
+  PrefillItem<NQT> it;
+  const int hb = p.Hq * p.B;
+  const int qblk = p.n_qblk - 1 - lin / hb;
+  const int rem = lin % hb;
+  it.h = rem % p.Hq;
+  it.b = rem / p.Hq;
+  it.hk = it.h / (p.Hq / p.Hkv);
+  it.q0 = qblk * (BM * NQT);
+  it.sp = p.start_pos_arr ? p.start_pos_arr[it.b] : p.start_pos;
+#pragma unroll
+  for (int t = 0; t < NQT; ++t) {
+    if (p.causal) {
+      const int last_row = min(it.q0 + (t + 1) * BM - 1, p.Tq - 1);
+      const long long kv_end = min((long long)p.Tk, (long long)it.sp + last_row + 1);
+      it.n_t[t] = kv_end <= 0 ? 0 : (int)((kv_end + BN - 1) / BN);
+    } else {
+      it.n_t[t] = (p.Tk + BN - 1) / BN;
+    }
+  }
+  it.n_kv = it.n_t[NQT - 1];
+  return it;
+}
+
 template <int D, int NQT>
 __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT>::CTAS_PER_SM)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -20,6 +58,9 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
                       const __grid_constant__ PrefillParams p) {
   using C = PrefillCfg<D, NQT>;
   constexpr int kEmuPairs = exp2_emu_pairs<D>();
+  // Warps that take every work item from the scheduler: the producer, the
+  // UMMA issuers and the softmax warps.
+  constexpr int kConsumerWarps = 1 + NQT + 4 * NQT;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
@@ -30,38 +71,30 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.err));
+  };
+  // The CTA's work item number n (n >= 1; item 0 is its own blockIdx.x),
+  // published by the scheduler warp in slot (n - 1) & 1: the blockIdx.x of a
+  // CTA it took over, or -1 when there is none (or on abort). Every consumer
+  // warp calls this once per item it finishes, in order.
+  auto next_item = [&](int n) -> int {
+    const int slot = (n - 1) & 1;
+    if (!wait_all(&bars->item_full[slot], (uint32_t)((n - 1) >> 1) & 1u)) return -1;
+    const int id = *reinterpret_cast<volatile int*>(&bars->item_id[slot]);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars->item_empty[slot]);
+    return id;
+  };
 
-  // Block -> (query block, head, batch). The heaviest causal query blocks are
-  // launched first; the Hq heads of one batch are adjacent so the query heads
-  // that share a KV head run together and re-read K/V from L2.
-  const int hb = p.Hq * p.B;
-  const int lin = blockIdx.x;
-  const int qblk = p.n_qblk - 1 - lin / hb;
-  const int rem = lin % hb;
-  const int h = rem % p.Hq;
-  const int b = rem / p.Hq;
-  const int hk = h / (p.Hq / p.Hkv);
-  const int q0 = qblk * (C::BM * C::NQT);
-  const int sp = p.start_pos_arr ? p.start_pos_arr[b] : p.start_pos;
-  // Key blocks each query tile needs: n_t[t] for tile t; tile 0 (earlier rows)
-  // never needs more blocks than tile 1, and under the causal mask at most one
-  // fewer. n_kv = n_t[1] is what gets loaded.
-  int n_t[C::NQT];
-#pragma unroll
-  for (int t = 0; t < C::NQT; ++t) {
-    if (p.causal) {
-      const int last_row = min(q0 + (t + 1) * C::BM - 1, p.Tq - 1);
-      const long long kv_end = min((long long)p.Tk, (long long)sp + last_row + 1);
-      n_t[t] = kv_end <= 0 ? 0 : (int)((kv_end + C::BN - 1) / C::BN);
-    } else {
-      n_t[t] = (p.Tk + C::BN - 1) / C::BN;
-    }
-  }
-  const int n_kv = n_t[C::NQT - 1];
-  const int n0 = n_t[0];
-
+  const PrefillItem<NQT> first = prefill_item<NQT>(p, blockIdx.x);
+  const int first_loads = min(C::STAGES, 2 * first.n_kv);
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
+    // Every UMMA issuer commits once its last S MMA of an item is issued;
+    // with o_tma each tile's epilogue also arrives once its staged output has
+    // been read by the TMA store (the staging buffer is the Q buffer).
+    mbar_init(&bars->q_free, C::NQT * (p.o_tma ? 2 : 1));
 #pragma unroll
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&bars->kv_full[s], 1);
@@ -77,30 +110,39 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
       mbar_init(&bars->o_full[t], 1);
     }
 #pragma unroll
-    for (int t = 0; t < C::NQT; ++t) mbar_init(&bars->drain[t], 1);
+    for (int t = 0; t < C::NQT; ++t) {
+      mbar_init(&bars->drain[t], 1);
+      mbar_init(&bars->staged[t], 4);
+    }
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->item_full[s], 1);
+      mbar_init(&bars->item_empty[s], kConsumerWarps);
+    }
+    mbar_init(&bars->clc_bar, 1);
     bars->abort_flag = 0;
     fence_mbar_init();
-    // The Q tiles and the first ring of K/V tiles are requested here, so
-    // their latency overlaps the TMEM allocation and the block barrier below
-    // (the producer warp issues the rest). The ring slots are all free.
-    if (n_kv > 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    // The first item's Q tiles and first ring of K/V tiles are requested
+    // here, so their latency overlaps the TMEM allocation and the block
+    // barrier below (the producer warp issues the rest). The ring is free.
+    if (first.n_kv > 0) {
       mbar_arrive_expect_tx(&bars->q_full, C::NQT * C::Q_TILE_BYTES);
 #pragma unroll
       for (int t = 0; t < C::NQT; ++t)
 #pragma unroll
         for (int c = 0; c < C::KCH; ++c)
           tma_load_4d(sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, &tm_q, &bars->q_full, c * 64,
-                      q0 + t * C::BM, h, b);
-      for (int i = 0; i < min(C::STAGES, 2 * n_kv); ++i) {
+                      first.q0 + t * C::BM, first.h, first.b);
+      for (int i = 0; i < first_loads; ++i) {
         uint8_t* dst = sKV + i * C::KV_TILE_BYTES;
         mbar_arrive_expect_tx(&bars->kv_full[i], C::KV_TILE_BYTES);
 #pragma unroll
         for (int c = 0; c < C::KCH; ++c)
           tma_load_4d(dst + c * C::CHUNK_BYTES, (i & 1) ? &tm_v : &tm_k, &bars->kv_full[i], c * 64,
-                      (i >> 1) * C::BN, hk, b);
+                      (i >> 1) * C::BN, first.hk, first.b);
       }
     }
   }
@@ -117,38 +159,76 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
   // budget, so the compiler allocates it against that budget.
   if (warp < 4) {
   setmaxnreg_dec<C::REGS_LOW>();
-  // The producer and the MMA issuer run as whole warps: every lane walks the
-  // loop and waits, one elected lane issues each copy / MMA / commit (the *_w
-  // helpers), which keeps the operands in uniform registers.
-  if (n_kv > 0 && warp == 0) {
+  // The producer, the MMA issuers and the scheduler run as whole warps:
+  // every lane walks the loop and waits, one elected lane issues each copy /
+  // MMA / commit (the *_w helpers), which keeps the operands in uniform
+  // registers.
+  if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // Q and the first STAGES K/V tiles were requested during set-up.
-    int issued = min(C::STAGES, 2 * n_kv);
-    for (int i = issued; i < 2 * n_kv; ++i) {
-      const int slot = i % C::STAGES;
-      const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->kv_empty[slot], ph ^ 1u, abort_flag, p.err))) break;
-      const int j = i >> 1;
-      const CUtensorMap* m = (i & 1) ? &tm_v : &tm_k;
-      uint8_t* dst = sKV + slot * C::KV_TILE_BYTES;
-      mbar_arrive_expect_tx_w(&bars->kv_full[slot], C::KV_TILE_BYTES);
+    // K/V loads run through the ring across work items: load g (counted
+    // from the CTA's first item) uses slot g % STAGES in round g / STAGES.
+    int lin = blockIdx.x;
+    int ld = 0;        // loads of earlier items
+    int issued = 0;    // loads issued in total
+    int q_rounds = 0;  // items with keys (one Q load each)
+    bool ok = true;
+    for (int n = 1;; ++n) {
+      const PrefillItem<NQT> it = prefill_item<NQT>(p, lin);
+      if (it.n_kv > 0) {
+        int i0 = 0;
+        if (n == 1) {
+          i0 = first_loads;  // requested during set-up
+          issued = first_loads;
+        } else {
+          // The Q buffer is free once every S MMA of the previous item with
+          // keys has completed (and its staged output has been stored).
+          if (!wait_all(&bars->q_free, (uint32_t)(q_rounds - 1) & 1u)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx_w(&bars->q_full, C::NQT * C::Q_TILE_BYTES);
 #pragma unroll
-      for (int c = 0; c < C::KCH; ++c)
-        tma_load_4d_w(dst + c * C::CHUNK_BYTES, m, &bars->kv_full[slot], c * 64, j * C::BN, hk, b);
-      issued = i + 1;
+          for (int t = 0; t < C::NQT; ++t)
+#pragma unroll
+            for (int c = 0; c < C::KCH; ++c)
+              tma_load_4d_w(sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, &tm_q, &bars->q_full, c * 64,
+                            it.q0 + t * C::BM, it.h, it.b);
+        }
+        ++q_rounds;
+        for (int i = i0; i < 2 * it.n_kv; ++i) {
+          const int g = ld + i;
+          const int slot = g % C::STAGES;
+          const uint32_t ph = (uint32_t)(g / C::STAGES) & 1u;
+          if (!wait_all(&bars->kv_empty[slot], ph ^ 1u)) {
+            ok = false;
+            break;
+          }
+          const CUtensorMap* m = (i & 1) ? &tm_v : &tm_k;
+          uint8_t* dst = sKV + slot * C::KV_TILE_BYTES;
+          mbar_arrive_expect_tx_w(&bars->kv_full[slot], C::KV_TILE_BYTES);
+#pragma unroll
+          for (int c = 0; c < C::KCH; ++c)
+            tma_load_4d_w(dst + c * C::CHUNK_BYTES, m, &bars->kv_full[slot], c * 64, (i >> 1) * C::BN, it.hk,
+                          it.b);
+          issued = g + 1;
+        }
+        if (!ok) break;
+        ld += 2 * it.n_kv;
+      }
+      lin = next_item(n);
+      if (lin < 0) break;
     }
     if (*abort_flag && lane == 0) {
       // Let every copy still in flight land before the CTA releases smem.
-      mbar_wait_quiet(&bars->q_full, 0);
-      for (int i = max(0, issued - C::STAGES); i < issued; ++i)
-        mbar_wait_quiet(&bars->kv_full[i % C::STAGES], (uint32_t)(i / C::STAGES) & 1u);
+      if (q_rounds > 0) mbar_wait_quiet(&bars->q_full, (uint32_t)(q_rounds - 1) & 1u);
+      for (int g = max(0, issued - C::STAGES); g < issued; ++g)
+        mbar_wait_quiet(&bars->kv_full[g % C::STAGES], (uint32_t)(g / C::STAGES) & 1u);
     }
-  } else if (n_kv > 0 && warp >= 1 && warp <= C::NQT) {
+  } else if (warp >= 1 && warp <= C::NQT) {
     // ------------------------------------------------------------ UMMA issuers
     // Warp 1 issues tile 0's MMAs, warp 2 (NQT = 2) tile 1's. Each reads
     // every K/V tile it needs and releases it (kv_empty counts NQT arrivals).
     const int t = warp - 1;
-    const int nt = t == 0 ? n0 : n_kv;
     constexpr uint32_t IDESC_S = umma_idesc_bf16(128, C::HALF, false);
     constexpr uint32_t IDESC_PV = umma_idesc_bf16(128, D, true);
     // Descriptors are built once; stepping through a tile adds the byte
@@ -182,73 +262,138 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
       for (int s = 4 * h; s < 4 * h + 4; ++s)
         umma_bf16_ts_w(dO, dS + pcol + 8 * s, va + (uint64_t)((s * 2048) >> 4), IDESC_PV, (acc || s > 0) ? 1u : 0u);
     };
-    auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.err));
-    };
-    auto wait_load = [&](int i) -> bool {
-      return wait_all(&bars->kv_full[i % C::STAGES], (uint32_t)(i / C::STAGES) & 1u);
-    };
 
-    // Per key block j: once the softmax has taken the second half of S_t(j),
-    // the first half of S_t(j+1) goes into its columns; once P_t(j) is
-    // published, PV_t(j) and then the second half of S_t(j+1) (over P_t(j)'s
-    // columns). V_j and K_{j+1} are waited for first (normally long landed).
-    // K/V load items are K_j = 2 j, V_j = 2 j + 1; `used` counts the items
-    // this warp has released so far, in order.
-    bool ok = wait_all(&bars->q_full, 0);
-    int used = 0;
-    if (ok && nt > 0) {
-      ok = wait_load(0);
-      if (ok) {
-        tc_fence_after();
-        issue_S_half(0, 0, 0);
-        tc_commit_w(&bars->sa_full[t]);
-        issue_S_half(0, 1, C::HALF);
-        tc_commit_w(&bars->sb_full[t]);
-        tc_commit_w(&bars->kv_empty[0]);
-        used = 1;
+    int lin = blockIdx.x;
+    int G = 0;         // ring position of the current item's first load
+    int J = 0;         // key blocks of this tile in earlier items (barrier rounds)
+    int q_rounds = 0;  // items with keys so far
+    bool ok = true;
+    for (int n = 1;; ++n) {
+      const PrefillItem<NQT> it = prefill_item<NQT>(p, lin);
+      const int nt = t == 0 ? it.n_t[0] : it.n_kv;
+      if (it.n_kv > 0) {
+        auto slot_of = [&](int i) { return (G + i) % C::STAGES; };
+        auto wait_load = [&](int i) -> bool {
+          return wait_all(&bars->kv_full[slot_of(i)], (uint32_t)((G + i) / C::STAGES) & 1u);
+        };
+        // Per key block j: once the softmax has taken the second half of
+        // S_t(j), the first half of S_t(j+1) goes into its columns; once
+        // P_t(j) is published, PV_t(j) and then the second half of S_t(j+1)
+        // (over P_t(j)'s columns). V_j and K_{j+1} are waited for first
+        // (normally long landed). K/V load items are K_j = 2 j,
+        // V_j = 2 j + 1; `used` counts the items this warp has released so
+        // far, in order. The previous item's last PV MMAs were issued by this
+        // thread before this item's S MMAs overwrite their P columns (UMMAs
+        // from one thread execute in order), and its O was read out by the
+        // softmax warps before they publish this item's first `mid`, which
+        // the first PV (the one that overwrites O) waits for.
+        ok = wait_all(&bars->q_full, (uint32_t)q_rounds & 1u);
+        ++q_rounds;
+        int used = 0;
+        if (ok && nt > 0) {
+          ok = wait_load(0);
+          if (ok) {
+            tc_fence_after();
+            issue_S_half(slot_of(0), 0, 0);
+            tc_commit_w(&bars->sa_full[t]);
+            issue_S_half(slot_of(0), 1, C::HALF);
+            tc_commit_w(&bars->sb_full[t]);
+            tc_commit_w(&bars->kv_empty[slot_of(0)]);
+            used = 1;
+            if (nt == 1) tc_commit_w(&bars->q_free);  // this item's last S MMA is issued
+          }
+        }
+        for (int j = 0; ok && j < nt; ++j) {
+          const uint32_t par = (uint32_t)(J + j) & 1u;
+          const int vslot = slot_of(2 * j + 1);
+          const bool next = j + 1 < nt;
+          const int kslot = slot_of(2 * j + 2);
+          const uint32_t fcol = (j & 1) ? C::HALF : 0;  // P_t(j), then S_t(j+1)'s second half
+          if (!wait_load(2 * j + 1) || (next && !wait_load(2 * j + 2))) {
+            ok = false;
+            break;
+          }
+          // Mid-block handoff: the next block's first S half (needed first by
+          // the softmax), then the first PV half.
+          if (!wait_all(&bars->mid[t], par)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (next) {
+            issue_S_half(kslot, 0, C::HALF - fcol);
+            tc_commit_w(&bars->sa_full[t]);
+          }
+          issue_PV_half(vslot, fcol, 0, j > 0);
+          tc_commit_w(&bars->pva_done[t]);
+          if (!wait_all(&bars->p_full[t], par)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_PV_half(vslot, fcol, 1, true);
+          tc_commit_w(&bars->kv_empty[vslot]);
+          if (next) {
+            issue_S_half(kslot, 1, fcol);
+            tc_commit_w(&bars->sb_full[t]);
+            tc_commit_w(&bars->kv_empty[kslot]);
+            used = 2 * j + 3;
+            if (j + 2 == nt) tc_commit_w(&bars->q_free);  // this item's last S MMA is issued
+          } else {
+            tc_commit_w(&bars->o_full[t]);
+            used = 2 * j + 2;
+          }
+        }
+        if (ok && nt == 0) tc_commit_w(&bars->q_free);  // this tile reads no Q in this item
+        // K/V tiles of blocks this tile never reaches (tile 0 stops one block
+        // short at the diagonal) are released once they have landed: landing
+        // means the slot is in the round of exactly that load.
+        for (int i = used; ok && i < 2 * it.n_kv; ++i) {
+          if (!wait_load(i)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) mbar_arrive(&bars->kv_empty[slot_of(i)]);
+        }
+        G += 2 * it.n_kv;
+        J += nt;
       }
-    }
-    for (int j = 0; ok && j < nt; ++j) {
-      const int vslot = (2 * j + 1) % C::STAGES;
-      const bool next = j + 1 < nt;
-      const int kslot = (2 * j + 2) % C::STAGES;
-      const uint32_t fcol = (j & 1) ? C::HALF : 0;  // P_t(j), then S_t(j+1)'s second half
-      if (!wait_load(2 * j + 1) || (next && !wait_load(2 * j + 2))) break;
-      // Mid-block handoff: the next block's first S half (needed first by
-      // the softmax), then the first PV half.
-      if (!wait_all(&bars->mid[t], (uint32_t)j & 1u)) break;
-      tc_fence_after();
-      if (next) {
-        issue_S_half(kslot, 0, C::HALF - fcol);
-        tc_commit_w(&bars->sa_full[t]);
-      }
-      issue_PV_half(vslot, fcol, 0, j > 0);
-      tc_commit_w(&bars->pva_done[t]);
-      if (!wait_all(&bars->p_full[t], (uint32_t)j & 1u)) break;
-      tc_fence_after();
-      issue_PV_half(vslot, fcol, 1, true);
-      tc_commit_w(&bars->kv_empty[vslot]);
-      if (next) {
-        issue_S_half(kslot, 1, fcol);
-        tc_commit_w(&bars->sb_full[t]);
-        tc_commit_w(&bars->kv_empty[kslot]);
-        used = 2 * j + 3;
-      } else {
-        tc_commit_w(&bars->o_full[t]);
-        used = 2 * j + 2;
-      }
-    }
-    // K/V tiles of blocks this tile never reaches (tile 0 stops one block
-    // short at the diagonal) are released once they have landed: landing
-    // means the slot is in the phase of exactly that tile.
-    for (int i = used; ok && i < 2 * n_kv; ++i) {
-      if (!wait_load(i)) break;
-      if (lane == 0) mbar_arrive(&bars->kv_empty[i % C::STAGES]);
+      if (!ok) break;
+      lin = next_item(n);
+      if (lin < 0) break;
     }
     // Every MMA issued above must finish before TMEM is deallocated.
     tc_commit_w(&bars->drain[t]);
     mbar_wait_quiet(&bars->drain[t], 0);
+  } else if (warp == 3) {
+    // ------------------------------------------------------------ scheduler
+    // Item n (n >= 1) is claimed once every consumer warp has taken item
+    // n - 1, i.e. has started working on it: one item of look-ahead, so the
+    // next Q and K/V can stream in early while the claim stays late enough
+    // for the last items to spread over the CTAs that finish first.
+    for (int n = 1;; ++n) {
+      if (n >= 2 && !wait_all(&bars->item_empty[(n - 2) & 1], (uint32_t)((n - 2) >> 1) & 1u)) break;
+      const uint32_t cpar = (uint32_t)(n - 1) & 1u;
+      if (lane == 0) {
+        fence_proxy_async_smem();  // the previous response was read through the generic proxy
+        mbar_arrive_expect_tx(&bars->clc_bar, 16);
+        clc_try_cancel(bars->clc_resp, &bars->clc_bar);
+      }
+      __syncwarp();
+      if (!wait_all(&bars->clc_bar, cpar)) {
+        // Abort: the response must still land before shared memory goes away.
+        if (lane == 0) mbar_wait_quiet(&bars->clc_bar, cpar);
+        break;
+      }
+      const int id = clc_cancelled_ctaid_x(bars->clc_resp);
+      __syncwarp();
+      if (lane == 0) {
+        bars->item_id[(n - 1) & 1] = id;
+        mbar_arrive(&bars->item_full[(n - 1) & 1]);
+      }
+      __syncwarp();
+      if (id < 0) break;
+    }
   }
   } else {
     setmaxnreg_inc<C::REGS_HIGH>();
@@ -259,143 +404,163 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     const uint32_t tR = tmem + lane_off + C::S_COL + t * C::BN;  // this row's S/P region
     const uint32_t tO = tmem + lane_off + C::O_COL + t * D;
-    const int grow = q0 + t * C::BM + row;
-    const bool valid = grow < p.Tq;
-    // Last visible key of this row (fits in int: it is below Tk).
-    const int kv_last = p.causal ? (int)min((long long)sp + grow, (long long)p.Tk - 1) : p.Tk - 1;
     const float sl2 = p.scale_log2;
-    float m_run = -INFINITY;
-    float l_run = 0.f;
+    int lin = blockIdx.x;
+    int J = 0;         // key blocks of this tile in earlier items (barrier rounds)
+    int o_rounds = 0;  // earlier items in which this tile had key blocks
     bool ok = true;
-    const int n_mine = t == 0 ? n0 : n_kv;
+    const uint32_t stage = smem_u32(sQ + t * C::Q_TILE_BYTES);
+    for (int n = 1;; ++n) {
+      const PrefillItem<NQT> it = prefill_item<NQT>(p, lin);
+      const int b = it.b, h = it.h;
+      const int grow = it.q0 + t * C::BM + row;
+      const bool valid = grow < p.Tq;
+      // Last visible key of this row (fits in int: it is below Tk).
+      const int kv_last = p.causal ? (int)min((long long)it.sp + grow, (long long)p.Tk - 1) : p.Tk - 1;
+      float m_run = -INFINITY;
+      float l_run = 0.f;
+      const int n_mine = t == 0 ? it.n_t[0] : it.n_kv;
 
-    for (int j = 0; j < n_mine; ++j) {
-      const uint32_t fcol = (j & 1) ? C::HALF : 0;  // first half of S_t(j); P_t(j) goes here
-      const uint32_t scol = C::HALF - fcol;         // second half of S_t(j)
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->sa_full[t], (uint32_t)j & 1u, abort_flag, p.err))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // Keys of block j past the row's last visible key are masked.
-      const int lim = kv_last - j * C::BN;
-      // One 64-key half at a time (64 registers of S): the first half's P
-      // is done while the second half may still be on the tensor core.
-      uint32_t s[2][32];
-      tmem_ld32(tR + fcol, s[0]);
-      tmem_ld32(tR + fcol + 32, s[1]);
-      tmem_wait_ld();
-      float hs0, hs1;
-      const float a0 = softmax_half_tmem<kEmuPairs>(s, lim, sl2, m_run, tR + fcol, hs0);
-      auto rescale_O = [&](float f) {
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + 32 * c, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * f);
-          tmem_st32(tO + 32 * c, o);
-        }
-      };
-      // Second half of S_t(j) (PV_t(j-1) is complete once it is, since it
-      // was issued after it).
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->sb_full[t], (uint32_t)j & 1u, abort_flag, p.err))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      if (j > 0 && __any_sync(0xffffffffu, a0 != 1.f)) {
-        // Rare: the running max moved; O (blocks < j) is brought to it before
-        // the first PV half adds block j.
-        rescale_O(a0);
-      }
-      tmem_ld32(tR + scol, s[0]);
-      tmem_ld32(tR + scol + 32, s[1]);
-      tmem_wait_ld();
-      // One handoff: P for keys 0-63 is in TMEM (the first PV half can go)
-      // and the second S half is in registers (its columns can take the
-      // first half of S_t(j+1)).
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->mid[t]);
-      const float a1 = softmax_half_tmem<kEmuPairs>(s, lim - C::HALF, sl2, m_run, tR + fcol + 32, hs1);
-      if (__any_sync(0xffffffffu, a1 != 1.f)) {
-        // Rare: the second half moved the running max. O then holds blocks
-        // < j and the first half of block j (once its PV half completes);
-        // bring it to the new max before the second PV half adds to it.
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars->pva_done[t], (uint32_t)j & 1u, abort_flag, p.err))) {
+      for (int j = 0; j < n_mine; ++j) {
+        const uint32_t par = (uint32_t)(J + j) & 1u;
+        const uint32_t fcol = (j & 1) ? C::HALF : 0;  // first half of S_t(j); P_t(j) goes here
+        const uint32_t scol = C::HALF - fcol;         // second half of S_t(j)
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->sa_full[t], par, abort_flag, p.err))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        rescale_O(a1);
-      }
-      l_run = (l_run * a0 + hs0) * a1 + hs1;
-
-      // P and any O rescale are in TMEM before the MMA may read them: every
-      // lane completes its stores and fences, then one arrive per warp.
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[t]);
-    }
-
-    if (n_mine == 0) {
-      if (valid) {
-        uint32_t z[32];
+        // Keys of block j past the row's last visible key are masked.
+        const int lim = kv_last - j * C::BN;
+        // One 64-key half at a time (64 registers of S): the first half's P
+        // is done while the second half may still be on the tensor core.
+        uint32_t s[2][32];
+        tmem_ld32(tR + fcol, s[0]);
+        tmem_ld32(tR + fcol + 32, s[1]);
+        tmem_wait_ld();
+        float hs0, hs1;
+        const float a0 = softmax_half_tmem<kEmuPairs>(s, lim, sl2, m_run, tR + fcol, hs0);
+        auto rescale_O = [&](float f) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) z[i] = 0u;
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + 32 * c, o);
+            tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) store_out_chunk(p, b, h, grow, c, z, 0.f);
-        if (p.lse) p.lse[((long long)b * p.Hq + h) * p.Tq + grow] = -INFINITY;
-      }
-    } else {
-      const bool w = ok && mbar_wait(&bars->o_full[t], 0, abort_flag, p.err);
-      // With o_tma the tile's rows are staged in its Q buffer, which no MMA
-      // reads any more (all of tile t's S MMAs completed before o_full[t]),
-      // and written out by one TMA store; rows past Tq are clipped by it.
-      const uint32_t stage = smem_u32(sQ + t * C::Q_TILE_BYTES);
-      if (__all_sync(0xffffffffu, w)) {
+            for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * f);
+            tmem_st32(tO + 32 * c, o);
+          }
+        };
+        // Second half of S_t(j) (PV_t(j-1) is complete once it is, since it
+        // was issued after it).
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->sb_full[t], par, abort_flag, p.err))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+        if (j > 0 && __any_sync(0xffffffffu, a0 != 1.f)) {
+          // Rare: the running max moved; O (blocks < j) is brought to it before
+          // the first PV half adds block j.
+          rescale_O(a0);
+        }
+        tmem_ld32(tR + scol, s[0]);
+        tmem_ld32(tR + scol + 32, s[1]);
+        tmem_wait_ld();
+        // One handoff: P for keys 0-63 is in TMEM (the first PV half can go)
+        // and the second S half is in registers (its columns can take the
+        // first half of S_t(j+1)).
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->mid[t]);
+        const float a1 = softmax_half_tmem<kEmuPairs>(s, lim - C::HALF, sl2, m_run, tR + fcol + 32, hs1);
+        if (__any_sync(0xffffffffu, a1 != 1.f)) {
+          // Rare: the second half moved the running max. O then holds blocks
+          // < j and the first half of block j (once its PV half completes);
+          // bring it to the new max before the second PV half adds to it.
+          if (!__all_sync(0xffffffffu, mbar_wait(&bars->pva_done[t], par, abort_flag, p.err))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          rescale_O(a1);
+        }
+        l_run = (l_run * a0 + hs0) * a1 + hs1;
+
+        // P and any O rescale are in TMEM before the MMA may read them: every
+        // lane completes its stores and fences, then one arrive per warp.
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full[t]);
+      }
+
+      if (n_mine == 0) {
+        if (valid) {
+          uint32_t z[32];
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + 32 * c, o);
-          tmem_wait_ld();
-          if (p.o_tma) {
-            float v[32];
-            if (valid) {
-              out_chunk_values(p, b, h, grow, c, o, inv_l, v);
-            } else {
+          for (int i = 0; i < 32; ++i) z[i] = 0u;
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          for (int c = 0; c < D / 32; ++c) store_out_chunk(p, b, h, grow, c, z, 0.f);
+          if (p.lse) p.lse[((long long)b * p.Hq + h) * p.Tq + grow] = -INFINITY;
+        }
+      } else {
+        const bool w = ok && mbar_wait(&bars->o_full[t], (uint32_t)o_rounds & 1u, abort_flag, p.err);
+        // With o_tma the tile's rows are staged in its Q buffer, which no MMA
+        // reads any more (all of tile t's S MMAs completed before o_full[t]),
+        // and written out by one TMA store; rows past Tq are clipped by it.
+        if (__all_sync(0xffffffffu, w)) {
+          tc_fence_after();
+          const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + 32 * c, o);
+            tmem_wait_ld();
+            if (p.o_tma) {
+              float v[32];
+              if (valid) {
+                out_chunk_values(p, b, h, grow, c, o, inv_l, v);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = 0.f;
+              }
+              stage_out_chunk_bf16(stage, C::CHUNK_BYTES, row, c, v);
+            } else if (valid) {
+              store_out_chunk(p, b, h, grow, c, o, inv_l);
             }
-            stage_out_chunk_bf16(stage, C::CHUNK_BYTES, row, c, v);
-          } else if (valid) {
-            store_out_chunk(p, b, h, grow, c, o, inv_l);
+          }
+          if (p.lse && valid) {
+            p.lse[((long long)b * p.Hq + h) * p.Tq + grow] =
+                l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994531f : -INFINITY;
           }
         }
-        if (p.lse && valid) {
-          p.lse[((long long)b * p.Hq + h) * p.Tq + grow] =
-              l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994531f : -INFINITY;
-        }
-      }
-      if (p.o_tma) {
-        // Every thread of the tile's warpgroup arrives here exactly once
-        // (this branch is tile-uniform), also on the abort path.
-        fence_proxy_async_smem();
-        named_bar_sync(1 + t, 128);
-        if (row == 0 && !*abort_flag) {
+        if (p.o_tma) {
+          // Each of the tile's four warps reports its staged rows (also on
+          // the abort path); row 0 waits for all four with a bounded wait and
+          // issues the store. The round is this tile's o_rounds.
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->staged[t]);
+          if (row == 0 && mbar_wait(&bars->staged[t], (uint32_t)o_rounds & 1u, abort_flag, p.err) &&
+              !*abort_flag) {
 #pragma unroll
-          for (int c = 0; c < C::KCH; ++c)
-            tma_store_4d(&tm_o, sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, c * 64, q0 + t * C::BM, h, b);
-          tma_store_commit();
-          tma_store_wait_read();  // the staging buffer must outlive the copy's reads
+            for (int c = 0; c < C::KCH; ++c)
+              tma_store_4d(&tm_o, sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, c * 64, it.q0 + t * C::BM, h,
+                           b);
+            tma_store_commit();
+            tma_store_wait_read();  // the staging buffer must outlive the copy's reads
+          }
         }
       }
+      // With o_tma the Q buffer is also this tile's output staging: the next
+      // item's Q may only land once the store above has read it.
+      if (p.o_tma && it.n_kv > 0 && row == 0) mbar_arrive(&bars->q_free);
+      J += n_mine;
+      if (n_mine > 0) ++o_rounds;
+      if (!ok) break;
+      lin = next_item(n);
+      if (lin < 0) break;
     }
   }
 

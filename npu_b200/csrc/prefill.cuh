@@ -9,14 +9,21 @@
 // reads key/value head h / (Hq / Hkv), the repeat_interleave mapping of
 // smollm.py:205-207, without materialising the expanded K/V.
 //
-// One CTA owns a 256-row query block of one (batch, query head): two 128-row
+// A work item is a 256-row query block of one (batch, query head): two 128-row
 // tiles that ping-pong on the tensor core, so one tile's softmax overlaps the
-// other tile's MMAs. Warp roles (12 warps):
+// other tile's MMAs. The grid has one CTA per work item, but a CTA does not
+// stop after its own: it takes over CTAs that have not started yet (cluster
+// launch control, clusterlaunchcontrol.try_cancel), in launch order, until
+// none is left. Each resident CTA thus walks items heaviest first, with its
+// TMEM, barriers and K/V ring set up once, the next item's K/V streaming in
+// while the current one finishes, and the next item's Q loaded and first S
+// MMAs issued while the current item's epilogue runs. Warp roles (12 warps):
 //   warp 0      TMA producer: Q once, then K_j / V_j tiles through a ring
 //   warp 1      TMEM owner + UMMA issuer for tile 0
 //   warp 2      UMMA issuer for tile 1 (each tile's MMAs wait only on that
 //               tile's softmax, so one tile's handoffs never stall the other's)
-//   warp 3      idle (keeps the softmax warpgroups warpgroup-aligned)
+//   warp 3      scheduler: claims the next work item (try_cancel) as soon as
+//               every role has started the current one
 //   warps 4-7   softmax + epilogue for tile 0 (thread = row = TMEM lane)
 //   warps 8-11  softmax + epilogue for tile 1
 // TMEM (512 columns): a 128-column S/P region per tile (R_t = [128 t,
@@ -84,7 +91,7 @@ struct PrefillCfg {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = OFF_Q + NQT * Q_TILE_BYTES;
   static constexpr int OFF_BAR = OFF_KV + STAGES * KV_TILE_BYTES;
-  static constexpr int BAR_BYTES = 256;
+  static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
   static constexpr int CTAS_PER_SM = NQT == 2 ? 1 : 2;
   static constexpr int TMEM_COLS = NQT == 2 ? 512 : 256;
@@ -110,6 +117,9 @@ struct PrefillCfg {
 // Barrier slots inside the OFF_BAR region.
 struct PrefillBars {
   uint64_t q_full;
+  uint64_t q_free;       // the Q buffer may be refilled for the next work
+                         // item: every S MMA of the current one has completed
+                         // (and, with o_tma, its output staged there is stored)
   uint64_t kv_full[8];
   uint64_t kv_empty[8];
   uint64_t sa_full[2];   // first 64-key half of S_t(j) is in TMEM
@@ -120,6 +130,16 @@ struct PrefillBars {
   uint64_t p_full[2];
   uint64_t o_full[2];
   uint64_t drain[2];     // per UMMA issuer warp
+  uint64_t staged[2];    // o_tma: the tile's four softmax warps have staged
+                         // their output rows (one arrive per warp)
+  // Work items beyond the CTA's own are taken from CTAs of the grid that have
+  // not started yet (cluster launch control); the scheduler warp publishes
+  // each one in a two-slot ring read by every other warp.
+  uint64_t item_full[2];
+  uint64_t item_empty[2];
+  uint64_t clc_bar;
+  alignas(16) uint8_t clc_resp[16];
+  int item_id[2];
   uint32_t tmem_base;
   int abort_flag;
 };

@@ -29,6 +29,7 @@ import torch.nn.functional as F
 
 from . import api
 from .kvcache import KVCache
+from .profiler import profile
 
 
 @dataclass
@@ -108,22 +109,26 @@ class SmolLMB200:
         c = self.cfg
         B, T, _ = h.shape
         Hq, Hkv, Dh = c.n_heads, c.n_kv_heads, c.head_dim
-        qkv = F.linear(h, lw["wqkv"])                                    # [B, T, (Hq + 2 Hkv) Dh]
+        with profile("qkv"):
+            qkv = F.linear(h, lw["wqkv"])                                # [B, T, (Hq + 2 Hkv) Dh]
         q = qkv[..., :Hq * Dh].view(B, T, Hq, Dh)
         k = qkv[..., Hq * Dh:(Hq + Hkv) * Dh].view(B, T, Hkv, Dh)
         v = qkv[..., (Hq + Hkv) * Dh:].view(B, T, Hkv, Dh)
         k_cache, v_cache = cache.layer(i)
-        q_rot = api.rope_append(q, k, v, self.cos, self.sin, k_cache, v_cache,
-                                start_pos_per_batch=cache.start, seqlens_out=cache.end)
+        with profile("rope"):
+            q_rot = api.rope_append(q, k, v, self.cos, self.sin, k_cache, v_cache,
+                                    start_pos_per_batch=cache.start, seqlens_out=cache.end)
         if T == 1:
-            o = api.decode(q_rot[:, :, 0], k_cache, v_cache, cache.end, out_dtype=h.dtype,
-                           workspace=self._workspace(B, cache.max_len))
+            with profile("attn"):
+                o = api.decode(q_rot[:, :, 0], k_cache, v_cache, cache.end, out_dtype=h.dtype,
+                               workspace=self._workspace(B, cache.max_len))
             return o.reshape(B, 1, Hq * Dh)
         # The kernel writes O straight into the [B, T, Hq * Dh] layout the
         # output projection reads (a strided [B, Hq, T, Dh] view of it).
         o = torch.empty((B, T, Hq, Dh), dtype=h.dtype, device=h.device)
-        api.prefill(q_rot, k_cache, v_cache, start_pos_per_batch=cache.start, scale=1.0 / math.sqrt(Dh),
-                    causal=True, out_dtype=h.dtype, out=o.transpose(1, 2))
+        with profile("attn"):
+            api.prefill(q_rot, k_cache, v_cache, start_pos_per_batch=cache.start, scale=1.0 / math.sqrt(Dh),
+                        causal=True, out_dtype=h.dtype, out=o.transpose(1, 2))
         return o.view(B, T, Hq * Dh)
 
     @torch.no_grad()
@@ -202,11 +207,20 @@ class SmolLMB200:
         if ids.dim() != 2 or ids.shape[0] != cache.batch:
             raise ValueError("ids must be [B, T] with B = cache.batch")
         x = self.embed[ids.to(self.device)]
+        # Op names follow the reference forward's profile() blocks
+        # (smollm.py:179-251), with "attn" for its attn_npu / attn_cpu.
         for i, lw in enumerate(self.layers):
-            h = rms_norm(x, lw["ln1"], c.rms_eps)
-            x = x + F.linear(self._attention(lw, h, cache, i), lw["wo"])
-            h = rms_norm(x, lw["ln2"], c.rms_eps)
-            x = x + F.linear(F.silu(F.linear(h, lw["w_gate"])) * F.linear(h, lw["w_up"]), lw["w_down"])
+            with profile("rms1"):
+                h = rms_norm(x, lw["ln1"], c.rms_eps)
+            a = self._attention(lw, h, cache, i)
+            with profile("wo"):
+                x = x + F.linear(a, lw["wo"])
+            with profile("rms2"):
+                h = rms_norm(x, lw["ln2"], c.rms_eps)
+            with profile("gate_up"):
+                gu = F.silu(F.linear(h, lw["w_gate"])) * F.linear(h, lw["w_up"])
+            with profile("w_down"):
+                x = x + F.linear(gu, lw["w_down"])
         cache.advance()
         x = rms_norm(x, self.final_norm, c.rms_eps)
         return F.linear(x, self.embed)

@@ -67,3 +67,34 @@ def test_run_batch_recognises_the_reference_block_layout():
     # single blocks (decode through run_batch) stay on the per-block path
     assert attn._units_of_blocks(k[:1], v[:1], [7]) == 1
     assert attn._units_of_blocks(k, v, [5, 5, 5, 5]) == 1
+
+
+def test_profiler_interface_and_disabled_noop():
+    """npu_b200.profiler keeps the reference profiler's interface
+    (npu/profiler.py): a shared no-op when disabled, per-name totals and call
+    counts when enabled, a report, and reset."""
+    from npu_b200.profiler import PROF, profile
+
+    PROF.reset()
+    PROF.disable()
+    assert profile("x") is profile("y")  # the shared no-op context manager
+    with profile("x"):
+        pass
+    assert PROF.stats() == {}
+    PROF.enable()
+    try:
+        for _ in range(3):
+            with profile("rms1"):
+                torch.ones(64).sum()
+        with profile("total"):
+            pass
+        st = PROF.stats()
+        assert st["rms1"]["calls"] == 3 and st["rms1"]["host_ms"] >= 0
+        assert st["total"]["calls"] == 1
+        if not torch.cuda.is_available():
+            assert st["rms1"]["device_ms"] is None
+        PROF.report()
+    finally:
+        PROF.disable()
+        PROF.reset()
+    assert PROF.stats() == {}

@@ -140,3 +140,27 @@ def test_smollm_prefill_step_as_cuda_graph(cuda_dev):
         assert torch.allclose(got, ref, atol=1e-4, rtol=0)
     assert graph_cache.lengths() == eager_cache.lengths() == [128, 128]
     assert api.device_error() == 0
+
+
+def test_profiler_times_the_forward_ops_on_the_device(cuda_dev):
+    """With the profiler on, a SmolLM forward on the B200 path records device
+    time (CUDA events) for each op name of the reference's profile() blocks
+    (smollm.py:179-251), 30 calls each, and the logits do not change."""
+    from npu_b200.profiler import PROF
+    from npu_b200.smollm_b200 import SmolLMB200, SmolLMConfig
+
+    model = SmolLMB200(make_state_dict(Config(), seed=0), SmolLMConfig(), cuda_dev)
+    ids = torch.randint(0, Config().vocab, (1, 64), generator=torch.Generator().manual_seed(3)).to(cuda_dev)
+    ref = model.forward(ids, model.new_cache(1, 128))
+    PROF.reset()
+    PROF.enable()
+    try:
+        got = model.forward(ids, model.new_cache(1, 128))
+        st = PROF.stats()
+    finally:
+        PROF.disable()
+        PROF.reset()
+    assert torch.equal(got, ref)
+    for name in ("rms1", "qkv", "rope", "attn", "wo", "rms2", "gate_up", "w_down"):
+        assert st[name]["calls"] == 30, name
+        assert st[name]["device_ms"] is not None and st[name]["device_ms"] > 0, name
