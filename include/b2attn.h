@@ -150,6 +150,26 @@ B2A_API int b2a_decode_gated(const void* q, const void* k_cache, const void* v_c
                              float scale, int split_len, int out_fp32, void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/*
+ * b2a_decode followed by the output projection and residual add, fused into
+ * the combine kernel: x[b, :] += o_b @ wo^T, where o_b is sequence b's
+ * attention output [Hq * D] (rounded to x's dtype) and wo [dim, Hq * D] the
+ * output projection weight (F.linear layout, row stride wo_ld elements, fp32
+ * with wo_fp32 = 1 else bf16; 16-byte aligned, wo_ld a multiple of 16 bytes).
+ * x: the residual stream [B, dim] (row stride x_sb elements, fp32 with
+ * x_fp32 = 1 else bf16), updated in place; the attention output itself is not
+ * stored. Replaces: the attention core plus `x = x + wo(o)` of the T=1 layer
+ * step (smollm.py:222-236, where the output projection follows attention at
+ * :235-236). Each query head's share is added with atomics, so the summation
+ * order (and the last bits of x) can differ from call to call. Workspace as
+ * b2a_decode.
+ */
+B2A_API int b2a_decode_proj(const void* q, const void* k_cache, const void* v_cache, const int* seqlens,
+                            const void* wo, long long wo_ld, int wo_fp32, int dim, void* x, long long x_sb,
+                            int x_fp32, int B, int Hq, int Hkv, int Lmax, int D, const long long* q_strides,
+                            const long long* k_strides, const long long* v_strides, float scale, int split_len,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
 /* Size of the fixed device scratch buffer behind b2a_decode_noalloc. */
 #define B2A_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 

@@ -276,6 +276,68 @@ def decode(
     return out
 
 
+def decode_proj(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    seqlens: torch.Tensor,
+    wo: torch.Tensor,
+    x: torch.Tensor,
+    *,
+    scale: Optional[float] = None,
+    split_len: int = 0,
+    workspace: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Decode attention fused with the output projection and residual add
+    (b2a_decode_proj): x += attention(q, caches) @ wo.T, in place.
+
+    q [B, Hq, D] and the caches as `decode`; wo [dim, Hq * D] (the F.linear
+    weight of the output projection, fp32 or bf16, last dim contiguous); x the
+    residual stream [B, dim] (fp32 or bf16, last dim contiguous), returned.
+    The attention output is rounded to x's dtype before the projection, as
+    the unfused `x + F.linear(o, wo)` would see it. Each query head's share is
+    added with atomics, so the last bits of x may differ between calls.
+    """
+    _need_cuda_bf16("q", q, 3)
+    _need_cuda_bf16("k_cache", k_cache, 4)
+    _need_cuda_bf16("v_cache", v_cache, 4)
+    B, Hq, D = q.shape
+    Bk, Hkv, Lmax, Dk = k_cache.shape
+    if (Bk, Dk) != (B, D) or tuple(v_cache.shape) != tuple(k_cache.shape):
+        raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k_cache.shape)} v{tuple(v_cache.shape)}")
+    if seqlens.dtype != torch.int32 or seqlens.device != q.device or seqlens.numel() != B:
+        raise ValueError("seqlens must be an int32 tensor [B] on q's device")
+    for name, t in (("wo", wo), ("x", x)):
+        if not isinstance(t, torch.Tensor) or t.device != q.device or t.dim() != 2 or t.stride(-1) != 1:
+            raise ValueError(f"{name} must be a 2-d CUDA tensor on q's device with a contiguous last dim")
+        if t.dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError(f"{name} must be float32 or bfloat16")
+    dim = wo.shape[0]
+    if wo.shape[1] != Hq * D or tuple(x.shape) != (B, dim):
+        raise ValueError(f"wo must be [dim, {Hq * D}] and x [{B}, dim], got wo{tuple(wo.shape)} x{tuple(x.shape)}")
+    seqlens = seqlens.contiguous()
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    lib = _lib.load()
+    if split_len == 0:
+        split_len = int(lib.b2a_decode_default_split(B, Hkv, Lmax))
+    need = int(lib.b2a_decode_workspace_bytes(B, Hq, Hkv, D, Lmax, split_len))
+    if need == 0:
+        raise _lib.B2AError(_lib.B2A_ERR_INVALID_ARG, "b2a_decode_workspace_bytes")
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        rc = lib.b2a_decode_proj(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), seqlens.data_ptr(), wo.data_ptr(),
+            wo.stride(0), 1 if wo.dtype == torch.float32 else 0, dim, x.data_ptr(), x.stride(0),
+            1 if x.dtype == torch.float32 else 0, B, Hq, Hkv, Lmax, D,
+            _lib.ll2(*q.stride()[:2]), _lib.ll3(*k_cache.stride()[:3]), _lib.ll3(*v_cache.stride()[:3]),
+            float(scale), int(split_len), workspace.data_ptr(), need, _stream_ptr(q.device),
+        )
+    _lib.check(rc, "b2a_decode_proj")
+    return x
+
+
 def rope_append(
     q: torch.Tensor,
     k: torch.Tensor,

@@ -275,19 +275,39 @@ int prefill_impl(const void* q, const void* k, const void* v, void* o, float* ls
   return rc ? B2A_ERR_LAUNCH : B2A_OK;
 }
 
+// Fused output projection of b2a_decode_proj (nullptr: plain decode).
+struct DecodeProj {
+  const void* wo;
+  long long wo_ld;
+  int dim, wo_fp32;
+  void* x;
+  long long x_sb;
+  int x_fp32;
+};
+
 int decode_impl(const void* q, const void* k_cache, const void* v_cache, const int* seqlens, void* o, int B,
                 int Hq, int Hkv, int Lmax, int D, const long long* qs, const long long* ks, const long long* vs,
                 const long long* os, float scale, int split_len, int out_fp32, void* workspace,
-                size_t workspace_bytes, const void* gate, const long long* gs, int gate_bf16, void* stream) {
-  if (!q || !k_cache || !v_cache || !seqlens || !o || !qs || !ks || !vs || !os) return B2A_ERR_INVALID_ARG;
+                size_t workspace_bytes, const void* gate, const long long* gs, int gate_bf16, void* stream,
+                const DecodeProj* proj = nullptr) {
+  if (!q || !k_cache || !v_cache || !seqlens || !qs || !ks || !vs) return B2A_ERR_INVALID_ARG;
+  if (!proj && (!o || !os)) return B2A_ERR_INVALID_ARG;
   if (!(scale > 0.f) || !std::isfinite(scale)) return B2A_ERR_INVALID_ARG;
   if (split_len == 0) split_len = b2a_decode_default_split(B, Hkv, Lmax);
   int group = 0, max_splits = 0;
   int rc = decode_geometry(B, Hq, Hkv, D, Lmax, split_len, &group, &max_splits);
   if (rc) return rc;
-  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(o)) return B2A_ERR_ALIGNMENT;
-  if (!strides_ok(qs, 2, 8) || !strides_ok(ks, 3, 8) || !strides_ok(vs, 3, 8) || !strides_ok(os, 2, 1))
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || (o && !aligned16(o))) return B2A_ERR_ALIGNMENT;
+  if (!strides_ok(qs, 2, 8) || !strides_ok(ks, 3, 8) || !strides_ok(vs, 3, 8) || (o && !strides_ok(os, 2, 1)))
     return B2A_ERR_ALIGNMENT;
+  if (proj) {
+    if (!proj->wo || !proj->x || proj->dim <= 0 || proj->wo_ld < (long long)Hq * D || proj->x_sb < proj->dim)
+      return B2A_ERR_INVALID_ARG;
+    // 16-byte vector reads of each weight row segment; element-aligned x.
+    if (!aligned16(proj->wo) || proj->wo_ld % (proj->wo_fp32 ? 4 : 8) ||
+        (reinterpret_cast<uintptr_t>(proj->x) & (proj->x_fp32 ? 3u : 1u)))
+      return B2A_ERR_ALIGNMENT;
+  }
   const size_t need = b2a_decode_workspace_bytes(B, Hq, Hkv, D, Lmax, split_len);
   if (!workspace || workspace_bytes < need || !aligned16(workspace)) return B2A_ERR_WORKSPACE;
 
@@ -307,8 +327,17 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
   p.part_o = static_cast<float*>(workspace);
   p.part_lse = reinterpret_cast<float*>(static_cast<char*>(workspace) + align256(n * D * sizeof(float)));
   p.o = o;
-  p.o_sb = os[0];
-  p.o_sh = os[1];
+  p.o_sb = o ? os[0] : 0;
+  p.o_sh = o ? os[1] : 0;
+  if (proj) {
+    p.wo = proj->wo;
+    p.wo_ld = proj->wo_ld;
+    p.dim = proj->dim;
+    p.wo_fp32 = proj->wo_fp32 ? 1 : 0;
+    p.x = proj->x;
+    p.x_sb = proj->x_sb;
+    p.x_fp32 = proj->x_fp32 ? 1 : 0;
+  }
   p.B = B;
   p.Hq = Hq;
   p.Hkv = Hkv;
@@ -426,6 +455,17 @@ int b2a_decode_gated(const void* q, const void* k_cache, const void* v_cache, co
   if (reinterpret_cast<uintptr_t>(gate) & (gate_bf16 ? 1u : 3u)) return B2A_ERR_ALIGNMENT;
   return decode_impl(q, k_cache, v_cache, seqlens, o, B, Hq, Hkv, Lmax, D, qs, ks, vs, os, scale, split_len,
                      out_fp32, workspace, workspace_bytes, gate, gs, gate_bf16, stream);
+}
+
+int b2a_decode_proj(const void* q, const void* k_cache, const void* v_cache, const int* seqlens, const void* wo,
+                    long long wo_ld, int wo_fp32, int dim, void* x, long long x_sb, int x_fp32, int B, int Hq,
+                    int Hkv, int Lmax, int D, const long long* qs, const long long* ks, const long long* vs,
+                    float scale, int split_len, void* workspace, size_t workspace_bytes, void* stream) {
+  const DecodeProj proj{wo, wo_ld, dim, wo_fp32, x, x_sb, x_fp32};
+  // The attention output is rounded to x's dtype before the projection, as
+  // an unfused caller storing it in the model dtype would.
+  return decode_impl(q, k_cache, v_cache, seqlens, nullptr, B, Hq, Hkv, Lmax, D, qs, ks, vs, nullptr, scale,
+                     split_len, x_fp32 ? 1 : 0, workspace, workspace_bytes, nullptr, nullptr, 0, stream, &proj);
 }
 
 int b2a_rope_append(const void* q, const void* k, const void* v, const long long* qs, const long long* ks,

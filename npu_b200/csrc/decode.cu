@@ -292,6 +292,7 @@ __global__ void __launch_bounds__(160)
 
 // One CTA per (sequence, query head); thread d owns output column d.
 __global__ void decode_combine_kernel(const __grid_constant__ DecodeParams p, int D) {
+  __shared__ float so[256];  // this head's output row, for the fused projection
   grid_dep_wait();  // every split's partials are written and visible
   const int bh = blockIdx.x;
   const int b = bh / p.Hq, h = bh % p.Hq;
@@ -318,11 +319,52 @@ __global__ void decode_combine_kernel(const __grid_constant__ DecodeParams p, in
                                    : static_cast<const float*>(p.gate)[gi];
       v *= __fdividef(1.f, 1.f + __expf(-gv));  // sigmoid, as torch.sigmoid in fp32
     }
-    const long long oi = (long long)b * p.o_sb + (long long)h * p.o_sh + d;
-    if (p.out_fp32)
-      reinterpret_cast<float*>(p.o)[oi] = v;
+    if (p.o) {
+      const long long oi = (long long)b * p.o_sb + (long long)h * p.o_sh + d;
+      if (p.out_fp32)
+        reinterpret_cast<float*>(p.o)[oi] = v;
+      else
+        reinterpret_cast<__nv_bfloat16*>(p.o)[oi] = __float2bfloat16_rn(v);
+    }
+    if (p.wo) so[d] = p.out_fp32 ? v : __bfloat162float(__float2bfloat16_rn(v));
+  }
+  if (!p.wo) return;
+  // Output projection of this head's share: x[b, n] += sum_d o[d] wo[n, h D + d]
+  // (o rounded to the attention output dtype first, as the unfused path's
+  // F.linear reads it). Thread n takes rows n, n + blockDim, ...: D
+  // contiguous weights each, read as 16-byte vectors.
+  __syncthreads();
+  const long long kb = (long long)h * D;
+  for (int n = threadIdx.x; n < p.dim; n += blockDim.x) {
+    float acc = 0.f;
+    if (p.wo_fp32) {
+      const float4* w = reinterpret_cast<const float4*>(static_cast<const float*>(p.wo) + n * p.wo_ld + kb);
+      for (int i = 0; i < D / 4; ++i) {
+        const float4 f = w[i];
+        acc = fmaf(so[4 * i], f.x, acc);
+        acc = fmaf(so[4 * i + 1], f.y, acc);
+        acc = fmaf(so[4 * i + 2], f.z, acc);
+        acc = fmaf(so[4 * i + 3], f.w, acc);
+      }
+    } else {
+      const uint4* w =
+          reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.wo) + n * p.wo_ld + kb);
+      for (int i = 0; i < D / 8; ++i) {
+        const uint4 u = w[i];
+        const uint32_t pr[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = __uint_as_float(pr[e] << 16), hi = __uint_as_float(pr[e] & 0xffff0000u);
+          acc = fmaf(so[8 * i + 2 * e], lo, acc);
+          acc = fmaf(so[8 * i + 2 * e + 1], hi, acc);
+        }
+      }
+    }
+    const long long xi = (long long)b * p.x_sb + n;
+    if (p.x_fp32)
+      atomicAdd(reinterpret_cast<float*>(p.x) + xi, acc);
     else
-      reinterpret_cast<__nv_bfloat16*>(p.o)[oi] = __float2bfloat16_rn(v);
+      atomicAdd(reinterpret_cast<__nv_bfloat16*>(p.x) + xi, __float2bfloat16_rn(acc));
   }
 }
 

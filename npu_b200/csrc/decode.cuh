@@ -22,6 +22,18 @@ struct DecodeParams {
   const void* gate;
   long long g_sb, g_sh;
   int gate_bf16;
+  // Optional fused output projection with residual add (b2a_decode_proj):
+  // x[b, :] += o_b @ wo^T, where o_b is sequence b's (gated) attention output
+  // flattened over heads, [Hq * D], and wo is [dim, Hq * D] with row stride
+  // wo_ld elements (the F.linear weight of the output projection). x is
+  // [B, dim] with row stride x_sb. Each combine CTA adds its query head's
+  // share with atomics; `o` is not written when it is nullptr.
+  const void* wo;
+  long long wo_ld;
+  int dim, wo_fp32;
+  void* x;
+  long long x_sb;
+  int x_fp32;
 };
 
 // Launch the split kernel and the LSE combine on `st`. Returns 0 on success,

@@ -66,8 +66,13 @@ def rope_tables(head_dim: int, max_pos: int, theta: float, dtype, device):
 class SmolLMB200:
     """Decoder stack over a KVCache; forward(ids, cache) -> logits."""
 
-    def __init__(self, sd: dict, cfg: SmolLMConfig, device: torch.device, dtype: Optional[torch.dtype] = None):
+    def __init__(self, sd: dict, cfg: SmolLMConfig, device: torch.device, dtype: Optional[torch.dtype] = None,
+                 fuse_wo: bool = True):
+        """fuse_wo: single-token steps run the output projection and residual
+        add inside the decode combine kernel (b2a_decode_proj) instead of a
+        separate GEMM."""
         dtype = dtype or sd["model.embed_tokens.weight"].dtype
+        self.fuse_wo = fuse_wo
         if dtype not in (torch.float32, torch.bfloat16):
             raise ValueError("the model runs in float32 or bfloat16")
         self.cfg, self.device, self.dtype = cfg, device, dtype
@@ -105,7 +110,9 @@ class SmolLMB200:
             self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         return self._ws
 
-    def _attention(self, lw: dict, h: torch.Tensor, cache: KVCache, i: int) -> torch.Tensor:
+    def _attention(self, lw: dict, h: torch.Tensor, cache: KVCache, i: int, x: torch.Tensor):
+        """Attention of layer i; returns the new residual stream (x plus the
+        output projection of the attention)."""
         c = self.cfg
         B, T, _ = h.shape
         Hq, Hkv, Dh = c.n_heads, c.n_kv_heads, c.head_dim
@@ -119,17 +126,28 @@ class SmolLMB200:
             q_rot = api.rope_append(q, k, v, self.cos, self.sin, k_cache, v_cache,
                                     start_pos_per_batch=cache.start, seqlens_out=cache.end)
         if T == 1:
+            # fp32 residual only: a bf16 stream would take one rounding per
+            # query head's atomic add instead of one per layer.
+            if self.fuse_wo and x.dtype == torch.float32 and x.is_contiguous():
+                # Attention, output projection and residual add in one decode
+                # (the combine kernel adds each head's share of x @ wo.T).
+                with profile("attn"):
+                    api.decode_proj(q_rot[:, :, 0], k_cache, v_cache, cache.end, lw["wo"], x.view(B, -1),
+                                    workspace=self._workspace(B, cache.max_len))
+                return x
             with profile("attn"):
                 o = api.decode(q_rot[:, :, 0], k_cache, v_cache, cache.end, out_dtype=h.dtype,
                                workspace=self._workspace(B, cache.max_len))
-            return o.reshape(B, 1, Hq * Dh)
+            with profile("wo"):
+                return x + F.linear(o.reshape(B, 1, Hq * Dh), lw["wo"])
         # The kernel writes O straight into the [B, T, Hq * Dh] layout the
         # output projection reads (a strided [B, Hq, T, Dh] view of it).
         o = torch.empty((B, T, Hq, Dh), dtype=h.dtype, device=h.device)
         with profile("attn"):
             api.prefill(q_rot, k_cache, v_cache, start_pos_per_batch=cache.start, scale=1.0 / math.sqrt(Dh),
                         causal=True, out_dtype=h.dtype, out=o.transpose(1, 2))
-        return o.view(B, T, Hq * Dh)
+        with profile("wo"):
+            return x + F.linear(o.view(B, T, Hq * Dh), lw["wo"])
 
     @torch.no_grad()
     def capture_decode(self, cache: KVCache, warmup: int = 2):
@@ -212,9 +230,7 @@ class SmolLMB200:
         for i, lw in enumerate(self.layers):
             with profile("rms1"):
                 h = rms_norm(x, lw["ln1"], c.rms_eps)
-            a = self._attention(lw, h, cache, i)
-            with profile("wo"):
-                x = x + F.linear(a, lw["wo"])
+            x = self._attention(lw, h, cache, i, x)
             with profile("rms2"):
                 h = rms_norm(x, lw["ln2"], c.rms_eps)
             with profile("gate_up"):

@@ -280,3 +280,26 @@ def test_noalloc_scratch_constant_and_checks_without_gpu():
         # config-4 geometry fits once the split is lengthened; without a GPU the
         # call then stops at the device lookup
         assert call(128, 32, 4, 32768, 128, 0) in (_lib.B2A_ERR_CUDA, _lib.B2A_ERR_DEVICE)
+
+
+def test_decode_proj_argument_validation():
+    """b2a_decode_proj rejects a missing or misaligned projection weight or
+    residual stream before any CUDA call."""
+    lib = _lib.load()
+
+    def call(wo=FAKE, wo_ld=8 * 128, w32=0, dim=576, x=FAKE, x_sb=576, x32=1, D=128, split=64):
+        return lib.b2a_decode_proj(FAKE, FAKE, FAKE, FAKE, wo, wo_ld, w32, dim, x, x_sb, x32, 2, 8, 2, 256, D,
+                                   _lib.ll2(8 * 128, 128), _lib.ll3(2 * 256 * 128, 256 * 128, 128),
+                                   _lib.ll3(2 * 256 * 128, 256 * 128, 128), 0.1, split, FAKE, 1 << 30, None)
+
+    assert call(wo=None) == _lib.B2A_ERR_INVALID_ARG
+    assert call(x=None) == _lib.B2A_ERR_INVALID_ARG
+    assert call(dim=0) == _lib.B2A_ERR_INVALID_ARG
+    assert call(wo_ld=100) == _lib.B2A_ERR_INVALID_ARG       # < Hq * D
+    assert call(x_sb=500) == _lib.B2A_ERR_INVALID_ARG        # < dim
+    assert call(wo=FAKE + 8) == _lib.B2A_ERR_ALIGNMENT
+    assert call(wo_ld=8 * 128 + 4) == _lib.B2A_ERR_ALIGNMENT  # bf16 rows not 16-byte aligned
+    assert call(x=FAKE + 2) == _lib.B2A_ERR_ALIGNMENT         # fp32 x
+    assert call(D=96) == _lib.B2A_ERR_HEAD_DIM
+    if not torch.cuda.is_available():
+        assert call() in (_lib.B2A_ERR_CUDA, _lib.B2A_ERR_DEVICE)

@@ -115,3 +115,35 @@ def test_config4_all_128_sequences(cuda_dev):
                            scale=1 / math.sqrt(D))
         err = (out[b:b + 1].float().cpu() - ref).abs().max().item()
         assert err <= TOL, (b, L, err)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B,Hq,Hkv,D,dim", [(3, 9, 3, 64, 576), (2, 16, 2, 256, 512)])
+def test_decode_proj_matches_decode_then_projection(cuda_dev, dtype, B, Hq, Hkv, D, dim):
+    """b2a_decode_proj (attention, output projection and residual add in the
+    combine kernel) against b2a_decode followed by x + F.linear(o, wo), and
+    against the fp32 oracle; SmolLM's (9/3 heads, 64, 576) and a Qwen-like
+    (16/2 heads, 256) geometry."""
+    import torch.nn.functional as F
+
+    from npu_b200 import api
+
+    Lmax = 700
+    lens = [1, 350, 700][:B]
+    q, kc, vc, sl = _case(B, Hq, Hkv, Lmax, D, lens, 61, cuda_dev)
+    q, kc, vc, sl = q.to(cuda_dev), kc.to(cuda_dev), vc.to(cuda_dev), sl.to(cuda_dev)
+    g = torch.Generator().manual_seed(62)
+    x0 = torch.randn(B, dim, generator=g).to(dtype).to(cuda_dev)
+    wo = (torch.randn(dim, Hq * D, generator=g) * 0.05).to(dtype).to(cuda_dev)
+    o = api.decode(q, kc, vc, sl, out_dtype=dtype)
+    want = (x0.float() + F.linear(o.reshape(B, Hq * D).float(), wo.float()))
+    x = x0.clone()
+    api.decode_proj(q, kc, vc, sl, wo, x)
+    assert api.device_error() == 0
+    scale = max(1.0, want.abs().max().item())
+    # fp32: summation order only; bf16: one rounding per query head's add
+    tol = 1e-4 if dtype == torch.float32 else 4e-2
+    assert (x.float() - want).abs().max().item() <= tol * scale
+    ref_o = A.decode_ref(q.cpu(), kc.cpu(), vc.cpu(), lens)
+    ref = x0.float().cpu() + ref_o.reshape(B, Hq * D) @ wo.float().cpu().T
+    assert (x.float().cpu() - ref).abs().max().item() <= (TOL if dtype == torch.float32 else 6e-2) * scale

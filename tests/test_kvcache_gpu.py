@@ -164,3 +164,28 @@ def test_profiler_times_the_forward_ops_on_the_device(cuda_dev):
     for name in ("rms1", "qkv", "rope", "attn", "wo", "rms2", "gate_up", "w_down"):
         assert st[name]["calls"] == 30, name
         assert st[name]["device_ms"] is not None and st[name]["device_ms"] > 0, name
+
+
+def test_smollm_decode_with_fused_output_projection(cuda_dev):
+    """Single-token steps with the output projection and residual add fused
+    into the decode combine kernel (b2a_decode_proj, the default for an fp32
+    model) give the logits of the unfused path (b2a_decode, then the wo
+    GEMM) over a prefill and 6 decode steps, and the same greedy tokens."""
+    from npu_b200 import api
+    from npu_b200.smollm_b200 import SmolLMB200, SmolLMConfig
+
+    sd = make_state_dict(Config(), seed=0)
+    fused = SmolLMB200(sd, SmolLMConfig(), cuda_dev)
+    plain = SmolLMB200(sd, SmolLMConfig(), cuda_dev, fuse_wo=False)
+    assert fused.fuse_wo and not plain.fuse_wo
+    ids = torch.randint(0, Config().vocab, (2, 50), generator=torch.Generator().manual_seed(12)).to(cuda_dev)
+    cf, cp = fused.new_cache(2, 128), plain.new_cache(2, 128)
+    lf, lp = fused.forward(ids, cf), plain.forward(ids, cp)
+    assert torch.equal(lf, lp)  # prefill takes the same path in both
+    tf = tp = lf[:, -1:].argmax(-1)
+    for _ in range(6):
+        lf, lp = fused.forward(tf, cf), plain.forward(tp, cp)
+        assert (lf - lp).abs().max().item() < 1e-3
+        tf, tp = lf[:, -1:].argmax(-1), lp[:, -1:].argmax(-1)
+        assert torch.equal(tf, tp)
+    assert api.device_error() == 0
