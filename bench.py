@@ -23,6 +23,9 @@ Sub-lines in the same JSON object:
                 D=64), device and end-to-end timings beside the CPU
                 restatements of fa_ref.py's flash_attention_ref and the dense
                 attention (replicas only)
+  chatbot       bench_chatbot.py's sweep on the B200 path (1 GPU): prefill,
+                decode step and sustained decode at L = 16 .. 2048 with top-1
+                against the CPU forward timed beside it
   config2       SmolLM2-135M 30-layer prefill forward at T=1024 on the GPU
                 (fp32 and bf16 weights) with the top-1 token checked against
                 the CPU forward, which is timed beside it; and one layer's
@@ -304,6 +307,7 @@ def run_ours(a, dist: Dist) -> dict | None:
     long_ctx = run_long_context(a, dist, dev, pk) if "long" in a.legs else None
     cfg1 = run_config1(a, dist, dev) if "config1" in a.legs else None
     cfg2 = run_config2(a, dist, dev) if "config2" in a.legs else None
+    chat = run_chatbot(a, dist, dev) if "chatbot" in a.legs else None
 
     cpu = None
     if rank == 0 and world == 1 and a.cpu_baseline and "prefill" in a.legs:
@@ -336,6 +340,7 @@ def run_ours(a, dist: Dist) -> dict | None:
         "long_context": long_ctx,
         "config1": cfg1,
         "config2": cfg2,
+        "chatbot": chat,
         "cpu_baseline": cpu,
     }
     return line
@@ -620,6 +625,116 @@ def run_config2(a, dist: Dist, dev) -> dict:
     return out
 
 
+def run_chatbot(a, dist: Dist, dev) -> dict | None:
+    """The reference's chatbot benchmark (bench_chatbot.py:61-136) on the B200
+    path: at each context length L, top-1 at position L-1 against the CPU
+    forward (correctness first), prefill latency, one decode step with the
+    context at L, and sustained greedy decode tok/s over `decode_n` tokens
+    (the decode step replayed as one CUDA graph). SmolLM2-135M with seeded
+    random weights (no checkpoint offline), fp32 as the reference's NPU
+    configuration; prompts as bench_chatbot.py:29-32 (seed 12345 + L). The CPU
+    side is the reference's layer restated (oracle), timed on all host cores,
+    up to `chatbot_cpu_max_L`. One GPU only (replicas would add nothing)."""
+    if dist.world != 1:
+        return None
+    from npu_b200.smollm_b200 import SmolLMB200, SmolLMConfig
+    from oracle.smollm_ref import Config, SmolLM, make_state_dict
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = Config()
+    sd = make_state_dict(cfg, seed=0)
+    gpu = SmolLMB200(sd, SmolLMConfig(), dev)
+    cpu = SmolLM(sd, cfg) if a.cpu_baseline else None
+    n = a.chatbot_decode_n
+    rows = []
+
+    def dev_ms(fn, iters):
+        ts = []
+        for _ in range(iters):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    def wall_ms(fn, iters):
+        ts = []
+        for _ in range(iters):
+            t0 = time.perf_counter()
+            fn()
+            ts.append((time.perf_counter() - t0) * 1e3)
+        return statistics.median(ts)
+
+    for L in a.chatbot_lengths:
+        ids = torch.randint(0, min(cfg.vocab, 32000), (1, L), generator=torch.Generator().manual_seed(12345 + L))
+        ids_d = ids.to(dev)
+        cache = gpu.new_cache(batch=1, max_len=L + n + 8)
+
+        def prefill():
+            cache.reset()
+            return gpu.forward(ids_d, cache)
+
+        logits = prefill()[0, -1].float().cpu()
+        prefill()
+        p_ms = dev_ms(prefill, a.steps)
+        prefill()
+        nxt = ids_d[:, -1:]
+        saved = cache._pos.clone()
+
+        def step():
+            cache._pos.copy_(saved)
+            return gpu.forward(nxt, cache)
+
+        step()
+        s_ms = dev_ms(step, a.steps)
+        cache._pos.copy_(saved)
+        graph_step = gpu.capture_decode(cache)
+
+        def decode_n():
+            cache._pos.copy_(saved)
+            tok = nxt
+            for _ in range(n):
+                tok = graph_step(tok)[:, -1].argmax(-1, keepdim=True)
+
+        decode_n()
+        d_ms = dev_ms(decode_n, max(1, a.steps // 2))
+        row = {"L": L, "prefill_ms": p_ms, "step_ms": s_ms, "decode_tok_s": n / (d_ms * 1e-3),
+               "top1": int(logits.argmax())}
+        del graph_step
+        if cpu is not None and L <= a.chatbot_cpu_max_L:
+            with torch.no_grad():
+                ref_logits, ref_cache = cpu.forward(ids)
+            ref = ref_logits[0, -1]
+            row["top1_matches_cpu"] = int(ref.argmax()) == row["top1"]
+            row["max_logit_delta"] = (logits - ref).abs().max().item()
+            it = 1 if L >= 1024 else 2
+            row["cpu_prefill_ms"] = wall_ms(lambda: cpu.forward(ids), it)
+            nid = ids[:, -1:]
+            row["cpu_step_ms"] = wall_ms(lambda: cpu.forward(nid, cache=ref_cache, start_pos=L), 3)
+
+            def cpu_decode():
+                c, tok, pos = ref_cache, nid, L
+                for _ in range(n):
+                    lg, c = cpu.forward(tok, cache=c, start_pos=pos)
+                    tok = lg[:, -1].argmax(-1, keepdim=True)
+                    pos += 1
+
+            row["cpu_decode_tok_s"] = n / (wall_ms(cpu_decode, 1) * 1e-3)
+        rows.append(row)
+        del cache
+    torch.cuda.empty_cache()
+    out = {"what": "bench_chatbot.py on the B200 path: TTFT (prefill), inter-token step, sustained greedy "
+                   "decode (CUDA graph per step), top-1 against the CPU forward",
+           "model": "SmolLM2-135M, seeded random weights, fp32", "decode_n": n, "rows": rows}
+    if cpu is not None:
+        checked = [r for r in rows if "top1_matches_cpu" in r]
+        out["correctness"] = f"{sum(r['top1_matches_cpu'] for r in checked)}/{len(checked)} lengths match top-1"
+        out["cpu_cores"] = torch.get_num_threads()
+    return out
+
+
 def load_traffic(key: str, **kw):
     """DRAM bytes per launch from the committed ncu summary (or None)."""
     p = ROOT / "profiles" / "traffic.json"
@@ -770,7 +885,7 @@ def run_reference(a) -> dict | None:
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-ALL_LEGS = {"prefill", "sweep", "decode", "long", "config1", "config2"}
+ALL_LEGS = {"prefill", "sweep", "decode", "long", "config1", "config2", "chatbot"}
 
 
 def main():
@@ -792,6 +907,10 @@ def main():
     ap.add_argument("--cpu-units", type=int, default=2)
     ap.add_argument("--cpu-decode-seqs", type=int, default=16)
     ap.add_argument("--cpu-long-blocks", type=int, default=4)
+    ap.add_argument("--chatbot-lengths", type=lambda s: [int(x) for x in s.split(",") if x],
+                    default=[16, 64, 256, 1024, 2048])
+    ap.add_argument("--chatbot-decode-n", type=int, default=16)
+    ap.add_argument("--chatbot-cpu-max-L", type=int, default=2048)
     a = ap.parse_args()
     if a.warmup < 3 and a.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
