@@ -215,9 +215,11 @@ int prefill_impl(const void* q, const void* k, const void* v, void* o, float* ls
       !strides_ok(os, 3, out_fp32 ? 4 : 8))
     return B2A_ERR_ALIGNMENT;
   if (gate && (!gs || !aligned16(gate) || !strides_ok(gs, 3, gate_bf16 ? 8 : 4))) return B2A_ERR_ALIGNMENT;
-  // Query rows per CTA: 128 for D = 256; for D <= 128 two 128-row tiles, or
-  // one for short sequences (prefill_rows_per_cta).
-  const int rows_per_cta = D == 256 ? 128 : b2a::prefill_rows_per_cta(D, Tq, Tk);
+  // Work items: 128 query rows for D = 256; for D <= 128 two 128-row tiles
+  // (two row blocks of one head, or one row block of two heads of a GQA
+  // group), or one tile for short sequences (prefill_plan).
+  const b2a::PrefillPlan plan = D == 256 ? b2a::PrefillPlan{128, 1, 0} : b2a::prefill_plan(D, Hq, Hkv, Tq, Tk);
+  const int rows_per_cta = plan.rows_per_item;
   const long long n_qblk = (Tq + rows_per_cta - 1) / rows_per_cta;
   if (n_qblk * Hq * (long long)B > 0x7fffffffLL) return B2A_ERR_INVALID_ARG;
 
@@ -238,7 +240,7 @@ int prefill_impl(const void* q, const void* k, const void* v, void* o, float* ls
   // which let the CTA exit without waiting for a copy (measured: TMA store
   // +3 % at T=512, -2 % at T=1024 there).
   CUtensorMap to = tq;
-  const int o_tma = (!out_fp32 && rows_per_cta == 128 && D != 256 &&
+  const int o_tma = (!out_fp32 && plan.tiles == 1 && D != 256 &&
                      tmap_bf16_4d(&to, o, D, Tq, Hq, B, os[2], os[1], os[0], 128) == B2A_OK)
                         ? 1
                         : 0;
@@ -260,6 +262,7 @@ int prefill_impl(const void* q, const void* k, const void* v, void* o, float* ls
   p.causal = causal ? 1 : 0;
   p.out_fp32 = out_fp32 ? 1 : 0;
   p.n_qblk = (int)n_qblk;
+  p.head_pairs = plan.head_pairs;
   p.err = err;
   p.gate = gate;
   if (gate) {
@@ -270,7 +273,7 @@ int prefill_impl(const void* q, const void* k, const void* v, void* o, float* ls
   }
   p.o_tma = o_tma;
   rc = D == 256 ? b2a::launch_prefill_d256(tq, tk, tv, p, static_cast<cudaStream_t>(stream))
-               : b2a::launch_prefill(D, rows_per_cta, tq, tk, tv, to, p, static_cast<cudaStream_t>(stream));
+               : b2a::launch_prefill(D, plan, tq, tk, tv, to, p, static_cast<cudaStream_t>(stream));
   if (rc == -3) return B2A_ERR_HEAD_DIM;
   return rc ? B2A_ERR_LAUNCH : B2A_OK;
 }

@@ -9,38 +9,63 @@ namespace b2a {
 #ifndef B2A_ONE_TILE_MAX_ROWS
 #define B2A_ONE_TILE_MAX_ROWS 1024
 #endif
-// Longest query length served by one-tile CTAs (prefill_rows_per_cta).
+// Longest query length served by one-tile CTAs (prefill_plan).
 constexpr int kOneTileMaxRows = B2A_ONE_TILE_MAX_ROWS;
+#ifndef B2A_HEAD_PAIRS
+#define B2A_HEAD_PAIRS 1
+#endif
+// Two-tile items pair query heads when the GQA group size is even.
+constexpr bool kHeadPairs = B2A_HEAD_PAIRS != 0;
 
 
-// Work item -> (query block, head, batch) and the key blocks its query tiles
-// need. The heaviest causal query blocks come first in launch order; the Hq
-// heads of one batch are adjacent so the query heads that share a KV head run
-// together and re-read K/V from L2.
+// Work item -> (query block, batch, heads) and the key blocks its query tiles
+// need. The heaviest causal query blocks come first in launch order; the
+// query heads that share a KV head are adjacent, so they run together and
+// re-read K/V from L2. Row mode: tile t covers rows [q0 + 128 t, +128) of
+// query head h. Head-pair mode (NQT = 2, head_pairs): tile t covers rows
+// [q0, q0 + 128) of query head h + t.
 template <int NQT>
 struct PrefillItem {
   int h, b, hk, q0, sp;
-  int n_t[NQT];  // key blocks query tile t needs; tile 0 (earlier rows) never
-                 // more than tile 1 and, under the causal mask, at most one fewer
+  int pairs;     // 1: head-pair item
+  int n_t[NQT];  // key blocks query tile t needs; tile 0 never more than
+                 // tile 1 and, under the causal mask, at most one fewer
   int n_kv;      // n_t[NQT - 1]: the key blocks that get loaded
+  __device__ __forceinline__ int head(int t) const { return h + (pairs ? t : 0); }
+  __device__ __forceinline__ int row0(int t) const { return q0 + (pairs ? 0 : 128 * t); }
 };
 
 template <int NQT>
 __device__ __forceinline__ PrefillItem<NQT> prefill_item(const PrefillParams& p, int lin) {
   constexpr int BM = 128, BN = 128;
   PrefillItem<NQT> it;
-  const int hb = p.Hq * p.B;
-  const int qblk = p.n_qblk - 1 - lin / hb;
-  const int rem = lin % hb;
-  it.h = rem % p.Hq;
-  it.b = rem / p.Hq;
-  it.hk = it.h / (p.Hq / p.Hkv);
-  it.q0 = qblk * (BM * NQT);
+  it.pairs = (NQT == 2 && p.head_pairs) ? 1 : 0;
+  int qblk;
+  if (it.pairs) {
+    const int np = p.Hq / p.Hkv / 2;  // head pairs per KV head
+    const int per = p.B * p.Hkv * np;
+    qblk = p.n_qblk - 1 - lin / per;
+    const int rem = lin % per;
+    const int pair = rem % np;
+    const int bk = rem / np;
+    it.hk = bk % p.Hkv;
+    it.b = bk / p.Hkv;
+    it.h = it.hk * (2 * np) + 2 * pair;
+    it.q0 = qblk * BM;
+  } else {
+    const int hb = p.Hq * p.B;
+    qblk = p.n_qblk - 1 - lin / hb;
+    const int rem = lin % hb;
+    it.h = rem % p.Hq;
+    it.b = rem / p.Hq;
+    it.hk = it.h / (p.Hq / p.Hkv);
+    it.q0 = qblk * (BM * NQT);
+  }
   it.sp = p.start_pos_arr ? p.start_pos_arr[it.b] : p.start_pos;
 #pragma unroll
   for (int t = 0; t < NQT; ++t) {
     if (p.causal) {
-      const int last_row = min(it.q0 + (t + 1) * BM - 1, p.Tq - 1);
+      const int last_row = min(it.row0(t) + BM - 1, p.Tq - 1);
       const long long kv_end = min((long long)p.Tk, (long long)it.sp + last_row + 1);
       it.n_t[t] = kv_end <= 0 ? 0 : (int)((kv_end + BN - 1) / BN);
     } else {
@@ -135,7 +160,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
 #pragma unroll
         for (int c = 0; c < C::KCH; ++c)
           tma_load_4d(sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, &tm_q, &bars->q_full, c * 64,
-                      first.q0 + t * C::BM, first.h, first.b);
+                      first.row0(t), first.head(t), first.b);
       for (int i = 0; i < first_loads; ++i) {
         uint8_t* dst = sKV + i * C::KV_TILE_BYTES;
         mbar_arrive_expect_tx(&bars->kv_full[i], C::KV_TILE_BYTES);
@@ -192,7 +217,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
 #pragma unroll
             for (int c = 0; c < C::KCH; ++c)
               tma_load_4d_w(sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, &tm_q, &bars->q_full, c * 64,
-                            it.q0 + t * C::BM, it.h, it.b);
+                            it.row0(t), it.head(t), it.b);
         }
         ++q_rounds;
         for (int i = i0; i < 2 * it.n_kv; ++i) {
@@ -412,8 +437,8 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
     const uint32_t stage = smem_u32(sQ + t * C::Q_TILE_BYTES);
     for (int n = 1;; ++n) {
       const PrefillItem<NQT> it = prefill_item<NQT>(p, lin);
-      const int b = it.b, h = it.h;
-      const int grow = it.q0 + t * C::BM + row;
+      const int b = it.b, h = it.head(t);
+      const int grow = it.row0(t) + row;
       const bool valid = grow < p.Tq;
       // Last visible key of this row (fits in int: it is below Tk).
       const int kv_last = p.causal ? (int)min((long long)it.sp + grow, (long long)p.Tk - 1) : p.Tk - 1;
@@ -546,8 +571,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
               !*abort_flag) {
 #pragma unroll
             for (int c = 0; c < C::KCH; ++c)
-              tma_store_4d(&tm_o, sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, c * 64, it.q0 + t * C::BM, h,
-                           b);
+              tma_store_4d(&tm_o, sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, c * 64, it.row0(t), h, b);
             tma_store_commit();
             tma_store_wait_read();  // the staging buffer must outlive the copy's reads
           }
@@ -585,23 +609,30 @@ static int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const 
   cudaFuncAttributes fa{};
   if (cudaFuncGetAttributes(&fa, fa_prefill_kernel<D, NQT>) != cudaSuccess || fa.numRegs < C::MIN_LAUNCH_REGS)
     return -1;
-  const long long nblk = (long long)p.n_qblk * p.Hq * p.B;
+  // One CTA per work item (query blocks x query heads, or x head pairs).
+  const long long nblk = (long long)p.n_qblk * p.B * (p.head_pairs ? p.Hq / 2 : p.Hq);
   if (nblk <= 0 || nblk > 0x7fffffffLL) return -2;
   fa_prefill_kernel<D, NQT><<<(unsigned)nblk, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, to, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 // One-tile CTAs (two per SM) pay off when a CTA sees few key blocks, so that
-// its start-up and epilogue are a large share of its time.
-int prefill_rows_per_cta(int D, int Tq, int Tk) {
+// its start-up and epilogue are a large share of its time. Two-tile items
+// pair query heads whenever the GQA group has an even size: both tiles then
+// walk the same key blocks (row-pair items leave tile 0 one block short on
+// the diagonal) and share every K/V tile.
+PrefillPlan prefill_plan(int D, int Hq, int Hkv, int Tq, int Tk) {
   (void)D;
   (void)Tk;
-  return Tq <= kOneTileMaxRows ? 128 : 256;
+  if (Tq <= kOneTileMaxRows) return PrefillPlan{128, 1, 0};
+  const bool even_group = Hkv > 0 && Hq % Hkv == 0 && (Hq / Hkv) % 2 == 0;
+  if (kHeadPairs && even_group) return PrefillPlan{128, 2, 1};
+  return PrefillPlan{256, 2, 0};
 }
 
-int launch_prefill(int D, int rows_per_cta, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                   const CUtensorMap& to, const PrefillParams& p, cudaStream_t st) {
-  const bool one = rows_per_cta == 128;
+int launch_prefill(int D, const PrefillPlan& plan, const CUtensorMap& tq, const CUtensorMap& tk,
+                   const CUtensorMap& tv, const CUtensorMap& to, const PrefillParams& p, cudaStream_t st) {
+  const bool one = plan.tiles == 1;
   switch (D) {
     case 64:
       return one ? launch_prefill_t<64, 1>(tq, tk, tv, to, p, st) : launch_prefill_t<64, 2>(tq, tk, tv, to, p, st);

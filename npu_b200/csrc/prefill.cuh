@@ -59,7 +59,12 @@ struct PrefillParams {
   float scale_log2;    // softmax scale * log2(e)
   int causal;
   int out_fp32;
-  int n_qblk;          // ceil(Tq / (128 * query tiles per CTA))
+  int n_qblk;          // query blocks per head: ceil(Tq / rows per work item)
+  // Two-tile work items (NQT = 2) pair query heads instead of row blocks:
+  // tile t is query head 2 i + t of a KV head's group over the same 128 rows,
+  // so both tiles walk the same key blocks and share every K/V tile. Needs an
+  // even group size (Hq / Hkv); n_qblk then counts 128-row blocks.
+  int head_pairs;
   int* err;            // device error word (may be nullptr)
   // Optional output gate [B, Hq, Tq, D] (element strides g_sb, g_sh, g_st,
   // innermost 1; fp32 or bf16): o = attention * sigmoid(gate), the gated
@@ -148,16 +153,23 @@ struct PrefillBars {
 int launch_prefill_d256(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                         const PrefillParams& p, cudaStream_t st);
 
-// Query rows per CTA the D <= 128 kernel will use for this problem (256 or
-// 128; PrefillParams::n_qblk must be computed with it).
-int prefill_rows_per_cta(int D, int Tq, int Tk);
+// How the D <= 128 kernel cuts this problem into work items: rows per item
+// and per query head (256 or 128: PrefillParams::n_qblk must be computed
+// with it) and whether two-tile items pair query heads (head_pairs, rows per
+// item then 128 with two tiles).
+struct PrefillPlan {
+  int rows_per_item;
+  int tiles;       // query tiles per CTA (NQT)
+  int head_pairs;
+};
+PrefillPlan prefill_plan(int D, int Hq, int Hkv, int Tq, int Tk);
 
-// Launch the prefill kernel on `st` with rows_per_cta query rows per CTA.
+// Launch the prefill kernel on `st` for the given plan.
 // Returns 0 on success, -3 for an unsupported head_dim, another negative
 // value on launch failure.
 // `to` describes O (4-D, 64-column x 128-row boxes, 128-byte swizzle) when
 // p.o_tma is set; it is not read otherwise.
-int launch_prefill(int D, int rows_per_cta, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                   const CUtensorMap& to, const PrefillParams& p, cudaStream_t st);
+int launch_prefill(int D, const PrefillPlan& plan, const CUtensorMap& tq, const CUtensorMap& tk,
+                   const CUtensorMap& tv, const CUtensorMap& to, const PrefillParams& p, cudaStream_t st);
 
 }  // namespace b2a

@@ -351,3 +351,24 @@ def test_config5_full_length_sampled_rows(cuda_dev):
         err = (out[0, h, rows].float().cpu() - ref).abs().max().item()
         assert err <= TOL, (h, err)
     assert not torch.isnan(out).any()
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(8, 2), (6, 2), (16, 16)])
+def test_two_tile_items_head_pairs_and_row_pairs(cuda_dev, Hq, Hkv):
+    """Queries longer than 1024 rows run as two-tile work items: two query
+    heads of one KV head over the same 128 rows when the GQA group is even
+    (8/2), else two 128-row blocks of one head (6/2 with group 3; 16/16 with
+    group 1). Ragged query length, a chunked start and the LSE, all rows
+    against the oracle."""
+    from npu_b200 import api
+
+    g = torch.Generator().manual_seed(40 + Hq)
+    B, Tq, Tk, D, sp = 2, 1300, 1500, 128, 200
+    q, k, v = _rand((B, Hq, Tq, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev)
+    out, lse = api.prefill(q, k, v, start_pos=sp, return_lse=True)
+    assert api.device_error() == 0
+    ref = A.dense_attention(q.cpu(), k.cpu(), v.cpu(), start_pos=sp)
+    assert (out.cpu() - ref).abs().max().item() <= TOL
+    s = (q.float().cpu() @ A.expand_kv(k.cpu().float(), Hq // Hkv).transpose(-1, -2)) / math.sqrt(D)
+    s = s.masked_fill(A.causal_mask(Tq, Tk, sp), float("-inf"))
+    assert (lse.cpu() - torch.logsumexp(s, dim=-1)).abs().max().item() < 1e-3
