@@ -160,9 +160,10 @@ B2A_API int b2a_decode_gated(const void* q, const void* k_cache, const void* v_c
  * x_fp32 = 1 else bf16), updated in place; the attention output itself is not
  * stored. Replaces: the attention core plus `x = x + wo(o)` of the T=1 layer
  * step (smollm.py:222-236, where the output projection follows attention at
- * :235-236). Each query head's share is added with atomics, so the summation
- * order (and the last bits of x) can differ from call to call. Workspace as
- * b2a_decode.
+ * :235-236). The combine runs per (block of 32 outputs, sequence): every
+ * output of x has one writer and a fixed summation order, so results are
+ * reproducible. Hq * D <= ~51k (one sequence's attention output in shared
+ * memory). Workspace as b2a_decode.
  */
 B2A_API int b2a_decode_proj(const void* q, const void* k_cache, const void* v_cache, const int* seqlens,
                             const void* wo, long long wo_ld, int wo_fp32, int dim, void* x, long long x_sb,

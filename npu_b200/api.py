@@ -295,8 +295,8 @@ def decode_proj(
     weight of the output projection, fp32 or bf16, last dim contiguous); x the
     residual stream [B, dim] (fp32 or bf16, last dim contiguous), returned.
     The attention output is rounded to x's dtype before the projection, as
-    the unfused `x + F.linear(o, wo)` would see it. Each query head's share is
-    added with atomics, so the last bits of x may differ between calls.
+    the unfused `x + F.linear(o, wo)` would see it; every output has one
+    writer and a fixed summation order (reproducible results).
     """
     _need_cuda_bf16("q", q, 3)
     _need_cuda_bf16("k_cache", k_cache, 4)

@@ -306,6 +306,9 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
   if (proj) {
     if (!proj->wo || !proj->x || proj->dim <= 0 || proj->wo_ld < (long long)Hq * D || proj->x_sb < proj->dim)
       return B2A_ERR_INVALID_ARG;
+    // The combine holds one sequence's attention output (Hq * D floats) in
+    // shared memory.
+    if (((long long)Hq * D + 2LL * Hq) * 4 > 200LL * 1024) return B2A_ERR_INVALID_ARG;
     // 16-byte vector reads of each weight row segment; element-aligned x.
     if (!aligned16(proj->wo) || proj->wo_ld % (proj->wo_fp32 ? 4 : 8) ||
         (reinterpret_cast<uintptr_t>(proj->x) & (proj->x_fp32 ? 3u : 1u)))
@@ -360,6 +363,7 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
   }
   rc = b2a::launch_decode(D, tk, tv, p, static_cast<cudaStream_t>(stream));
   if (rc == -3) return B2A_ERR_HEAD_DIM;
+  if (rc == -4) return B2A_ERR_INVALID_ARG;
   return rc ? B2A_ERR_LAUNCH : B2A_OK;
 }
 

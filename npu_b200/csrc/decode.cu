@@ -292,7 +292,6 @@ __global__ void __launch_bounds__(160)
 
 // One CTA per (sequence, query head); thread d owns output column d.
 __global__ void decode_combine_kernel(const __grid_constant__ DecodeParams p, int D) {
-  __shared__ float so[256];  // this head's output row, for the fused projection
   grid_dep_wait();  // every split's partials are written and visible
   const int bh = blockIdx.x;
   const int b = bh / p.Hq, h = bh % p.Hq;
@@ -326,45 +325,79 @@ __global__ void decode_combine_kernel(const __grid_constant__ DecodeParams p, in
       else
         reinterpret_cast<__nv_bfloat16*>(p.o)[oi] = __float2bfloat16_rn(v);
     }
-    if (p.wo) so[d] = p.out_fp32 ? v : __bfloat162float(__float2bfloat16_rn(v));
   }
-  if (!p.wo) return;
-  // Output projection of this head's share: x[b, n] += sum_d o[d] wo[n, h D + d]
-  // (o rounded to the attention output dtype first, as the unfused path's
-  // F.linear reads it). Thread n takes rows n, n + blockDim, ...: D
-  // contiguous weights each, read as 16-byte vectors.
+}
+
+// Combine fused with the output projection and residual add (b2a_decode_proj):
+// one CTA per (block of PROJ_N outputs, sequence). It merges the splits of
+// every query head of its sequence into the attention output o [Hq * D]
+// (shared memory; the same per-element arithmetic as decode_combine_kernel,
+// then rounded to x's dtype), and adds o @ wo^T for its outputs into the
+// residual stream: warp w takes outputs n0 + w, n0 + w + 4, ..., its lanes
+// stride over o and the weight row, and a fixed shuffle tree sums them. Every
+// output has one writer and a fixed summation order, so the result does not
+// depend on scheduling.
+constexpr int kProjN = 32;  // outputs per CTA
+constexpr int kProjMaxSmem = 200 * 1024;  // attention output row of one sequence, Hq * D floats
+
+__global__ void decode_combine_proj_kernel(const __grid_constant__ DecodeParams p, int D) {
+  extern __shared__ float sm_proj[];
+  grid_dep_wait();  // every split's partials are written and visible
+  const int b = blockIdx.y;
+  const int HD = p.Hq * D;
+  float* so = sm_proj;             // [Hq * D] attention output of sequence b
+  float* sM = so + HD;             // [Hq] per-head max LSE (log2 domain)
+  float* sW = sM + p.Hq;           // [Hq] per-head sum of split weights
+  int L = p.seqlens[b];
+  L = L < 0 ? 0 : (L > p.Lmax ? p.Lmax : L);
+  int ns = (L + p.split_len - 1) / p.split_len;
+  ns = ns > p.max_splits ? p.max_splits : ns;
+  for (int h = threadIdx.x; h < p.Hq; h += blockDim.x) {
+    const int g = h / p.group, r = h % p.group;
+    const long long base = ((long long)b * p.Hkv + g) * p.max_splits;
+    float M = -INFINITY;
+    for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, p.part_lse[(base + sp) * p.group + r]);
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    float wsum = 0.f;
+    for (int sp = 0; sp < ns; ++sp) wsum += ex2(p.part_lse[(base + sp) * p.group + r] - Mu);
+    sM[h] = Mu;
+    sW[h] = wsum;
+  }
   __syncthreads();
-  const long long kb = (long long)h * D;
-  for (int n = threadIdx.x; n < p.dim; n += blockDim.x) {
+  for (int e = threadIdx.x; e < HD; e += blockDim.x) {
+    const int h = e / D, d = e % D;
+    const int g = h / p.group, r = h % p.group;
+    const long long base = ((long long)b * p.Hkv + g) * p.max_splits;
+    float osum = 0.f;
+    for (int sp = 0; sp < ns; ++sp)
+      osum += ex2(p.part_lse[(base + sp) * p.group + r] - sM[h]) * p.part_o[((base + sp) * p.group + r) * D + d];
+    const float v = sW[h] > 0.f ? osum / sW[h] : 0.f;
+    so[e] = p.x_fp32 ? v : __bfloat162float(__float2bfloat16_rn(v));
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const int n0 = blockIdx.x * kProjN;
+  for (int n = n0 + warp; n < min(n0 + kProjN, p.dim); n += nwarps) {
     float acc = 0.f;
     if (p.wo_fp32) {
-      const float4* w = reinterpret_cast<const float4*>(static_cast<const float*>(p.wo) + n * p.wo_ld + kb);
-      for (int i = 0; i < D / 4; ++i) {
-        const float4 f = w[i];
-        acc = fmaf(so[4 * i], f.x, acc);
-        acc = fmaf(so[4 * i + 1], f.y, acc);
-        acc = fmaf(so[4 * i + 2], f.z, acc);
-        acc = fmaf(so[4 * i + 3], f.w, acc);
-      }
+      const float* w = static_cast<const float*>(p.wo) + (long long)n * p.wo_ld;
+      for (int k = lane; k < HD; k += 32) acc = fmaf(so[k], w[k], acc);
     } else {
-      const uint4* w =
-          reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.wo) + n * p.wo_ld + kb);
-      for (int i = 0; i < D / 8; ++i) {
-        const uint4 u = w[i];
-        const uint32_t pr[4] = {u.x, u.y, u.z, u.w};
+      const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(p.wo) + (long long)n * p.wo_ld;
+      for (int k = lane; k < HD; k += 32) acc = fmaf(so[k], __bfloat162float(w[k]), acc);
+    }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float lo = __uint_as_float(pr[e] << 16), hi = __uint_as_float(pr[e] & 0xffff0000u);
-          acc = fmaf(so[8 * i + 2 * e], lo, acc);
-          acc = fmaf(so[8 * i + 2 * e + 1], hi, acc);
-        }
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) {
+      const long long xi = (long long)b * p.x_sb + n;
+      if (p.x_fp32) {
+        float* xp = reinterpret_cast<float*>(p.x) + xi;
+        *xp = *xp + acc;
+      } else {
+        __nv_bfloat16* xp = reinterpret_cast<__nv_bfloat16*>(p.x) + xi;
+        *xp = __float2bfloat16_rn(__bfloat162float(*xp) + acc);
       }
     }
-    const long long xi = (long long)b * p.x_sb + n;
-    if (p.x_fp32)
-      atomicAdd(reinterpret_cast<float*>(p.x) + xi, acc);
-    else
-      atomicAdd(reinterpret_cast<__nv_bfloat16*>(p.x) + xi, __float2bfloat16_rn(acc));
   }
 }
 
@@ -391,6 +424,19 @@ static int launch_decode_t(const CUtensorMap& tk, const CUtensorMap& tv, const D
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, decode_split_kernel<D>, tk, tv, p) != cudaSuccess) return -1;
+  if (p.wo) {
+    const size_t smem = ((size_t)p.Hq * D + 2 * (size_t)p.Hq) * sizeof(float);
+    if (smem > (size_t)kProjMaxSmem) return -4;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(decode_combine_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return -1;
+    cfg.gridDim = dim3((unsigned)((p.dim + kProjN - 1) / kProjN), (unsigned)p.B);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    if (cudaLaunchKernelEx(&cfg, decode_combine_proj_kernel, p, D) != cudaSuccess) return -1;
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  }
   cfg.gridDim = dim3((unsigned)(p.B * p.Hq));
   cfg.blockDim = dim3(D < 128 ? 64 : 128);
   cfg.dynamicSmemBytes = 0;

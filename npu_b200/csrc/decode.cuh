@@ -26,8 +26,9 @@ struct DecodeParams {
   // x[b, :] += o_b @ wo^T, where o_b is sequence b's (gated) attention output
   // flattened over heads, [Hq * D], and wo is [dim, Hq * D] with row stride
   // wo_ld elements (the F.linear weight of the output projection). x is
-  // [B, dim] with row stride x_sb. Each combine CTA adds its query head's
-  // share with atomics; `o` is not written when it is nullptr.
+  // [B, dim] with row stride x_sb. The combine then runs per (block of
+  // outputs, sequence) and each output has one writer; `o` is not written
+  // when it is nullptr.
   const void* wo;
   long long wo_ld;
   int dim, wo_fp32;
@@ -37,7 +38,8 @@ struct DecodeParams {
 };
 
 // Launch the split kernel and the LSE combine on `st`. Returns 0 on success,
-// -3 for an unsupported head_dim, another negative value on launch failure.
+// -3 for an unsupported head_dim, -4 for a fused projection whose attention
+// row does not fit in shared memory, another negative value on launch failure.
 int launch_decode(int D, const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p, cudaStream_t st);
 
 }  // namespace b2a

@@ -14,8 +14,10 @@ constexpr int kOneTileMaxRows = B2A_ONE_TILE_MAX_ROWS;
 #ifndef B2A_HEAD_PAIRS
 #define B2A_HEAD_PAIRS 1
 #endif
-// Two-tile items pair query heads when the GQA group size is even.
+// Two-tile items pair query heads when the GQA group size is even and the
+// query is at most this long; longer queries use row-pair items.
 constexpr bool kHeadPairs = B2A_HEAD_PAIRS != 0;
+constexpr int kHeadPairMaxRows = 3072;
 
 
 // Work item -> (query block, batch, heads) and the key blocks its query tiles
@@ -42,12 +44,29 @@ __device__ __forceinline__ PrefillItem<NQT> prefill_item(const PrefillParams& p,
   it.pairs = (NQT == 2 && p.head_pairs) ? 1 : 0;
   int qblk;
   if (it.pairs) {
+    // Items come in super blocks of two adjacent 128-row blocks, heaviest
+    // first; inside one, the 2 x np items of a KV head (both row blocks of
+    // every head pair) are adjacent, so the CTAs in flight at any time cover
+    // as few KV heads as in row mode (one 256-row block of every query head
+    // of the group) and their K/V stay in L2. With an odd number of row
+    // blocks the last super block holds row block 0 only.
     const int np = p.Hq / p.Hkv / 2;  // head pairs per KV head
     const int per = p.B * p.Hkv * np;
-    qblk = p.n_qblk - 1 - lin / per;
-    const int rem = lin % per;
-    const int pair = rem % np;
-    const int bk = rem / np;
+    const int full = p.n_qblk / 2;    // super blocks with two row blocks
+    int pair, bk;
+    if (lin < full * 2 * per) {
+      const int g = lin / (2 * per);
+      const int rem = lin % (2 * per);
+      const int inner = rem % (2 * np);
+      bk = rem / (2 * np);
+      pair = inner % np;
+      qblk = p.n_qblk - 1 - (2 * g + inner / np);
+    } else {
+      const int rem = lin - full * 2 * per;
+      pair = rem % np;
+      bk = rem / np;
+      qblk = 0;
+    }
     it.hk = bk % p.Hkv;
     it.b = bk / p.Hkv;
     it.h = it.hk * (2 * np) + 2 * pair;
@@ -617,16 +636,20 @@ static int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const 
 }
 
 // One-tile CTAs (two per SM) pay off when a CTA sees few key blocks, so that
-// its start-up and epilogue are a large share of its time. Two-tile items
-// pair query heads whenever the GQA group has an even size: both tiles then
-// walk the same key blocks (row-pair items leave tile 0 one block short on
-// the diagonal) and share every K/V tile.
+// its start-up and epilogue are a large share of its time. Between that and
+// kHeadPairMaxRows, two-tile items pair query heads when the GQA group size is
+// even: both tiles then walk the same key blocks, where row-pair items leave
+// tile 0 one block short on the diagonal, which at ~9 key blocks per item
+// (T = 2048) costs ~10 %. Measured on B200 (config 3 heads, TFLOP/s, head
+// pairs against row pairs, three passes): T=2048 853-893 against 784-826,
+// T=4096 982-992 against 1003-1038, T=8192 987-990 against 998-1002; at
+// T <= 1024 head-pair two-tile items were no faster than one-tile CTAs.
 PrefillPlan prefill_plan(int D, int Hq, int Hkv, int Tq, int Tk) {
   (void)D;
   (void)Tk;
   if (Tq <= kOneTileMaxRows) return PrefillPlan{128, 1, 0};
   const bool even_group = Hkv > 0 && Hq % Hkv == 0 && (Hq / Hkv) % 2 == 0;
-  if (kHeadPairs && even_group) return PrefillPlan{128, 2, 1};
+  if (kHeadPairs && even_group && Tq <= kHeadPairMaxRows) return PrefillPlan{128, 2, 1};
   return PrefillPlan{256, 2, 0};
 }
 

@@ -126,11 +126,9 @@ class SmolLMB200:
             q_rot = api.rope_append(q, k, v, self.cos, self.sin, k_cache, v_cache,
                                     start_pos_per_batch=cache.start, seqlens_out=cache.end)
         if T == 1:
-            # fp32 residual only: a bf16 stream would take one rounding per
-            # query head's atomic add instead of one per layer.
-            if self.fuse_wo and x.dtype == torch.float32 and x.is_contiguous():
+            if self.fuse_wo and x.is_contiguous():
                 # Attention, output projection and residual add in one decode
-                # (the combine kernel adds each head's share of x @ wo.T).
+                # (the combine kernel adds o @ wo.T into x in place).
                 with profile("attn"):
                     api.decode_proj(q_rot[:, :, 0], k_cache, v_cache, cache.end, lw["wo"], x.view(B, -1),
                                     workspace=self._workspace(B, cache.max_len))

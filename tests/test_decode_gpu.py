@@ -141,9 +141,13 @@ def test_decode_proj_matches_decode_then_projection(cuda_dev, dtype, B, Hq, Hkv,
     api.decode_proj(q, kc, vc, sl, wo, x)
     assert api.device_error() == 0
     scale = max(1.0, want.abs().max().item())
-    # fp32: summation order only; bf16: one rounding per query head's add
-    tol = 1e-4 if dtype == torch.float32 else 4e-2
+    # fp32: summation order only; bf16: the residual add rounded once
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
     assert (x.float() - want).abs().max().item() <= tol * scale
+    # one writer per output and a fixed summation order: reproducible
+    x2 = x0.clone()
+    api.decode_proj(q, kc, vc, sl, wo, x2)
+    assert torch.equal(x, x2)
     ref_o = A.decode_ref(q.cpu(), kc.cpu(), vc.cpu(), lens)
     ref = x0.float().cpu() + ref_o.reshape(B, Hq * D) @ wo.float().cpu().T
     assert (x.float().cpu() - ref).abs().max().item() <= (TOL if dtype == torch.float32 else 6e-2) * scale

@@ -168,9 +168,9 @@ def test_profiler_times_the_forward_ops_on_the_device(cuda_dev):
 
 def test_smollm_decode_with_fused_output_projection(cuda_dev):
     """Single-token steps with the output projection and residual add fused
-    into the decode combine kernel (b2a_decode_proj, the default for an fp32
-    model) give the logits of the unfused path (b2a_decode, then the wo
-    GEMM) over a prefill and 6 decode steps, and the same greedy tokens."""
+    into the decode combine kernel (b2a_decode_proj, the default) give the
+    logits of the unfused path (b2a_decode, then the wo GEMM) over a prefill
+    and 6 decode steps, and the same greedy tokens."""
     from npu_b200 import api
     from npu_b200.smollm_b200 import SmolLMB200, SmolLMConfig
 
