@@ -9,9 +9,11 @@
 // reads key/value head h / (Hq / Hkv), the repeat_interleave mapping of
 // smollm.py:205-207, without materialising the expanded K/V.
 //
-// A work item is a 256-row query block of one (batch, query head): two 128-row
-// tiles that ping-pong on the tensor core, so one tile's softmax overlaps the
-// other tile's MMAs. The grid has one CTA per work item, but a CTA does not
+// A work item is two 128-row query tiles that ping-pong on the tensor core,
+// so one tile's softmax overlaps the other tile's MMAs: a 256-row query block
+// of one (batch, query head), or, for queries of 1025-3072 rows with an even
+// GQA group, the same 128 rows of two query heads that share a KV head (both
+// tiles then walk the same key blocks). The grid has one CTA per work item, but a CTA does not
 // stop after its own: it takes over CTAs that have not started yet (cluster
 // launch control, clusterlaunchcontrol.try_cancel), in launch order, until
 // none is left. Each resident CTA thus walks items heaviest first, with its
