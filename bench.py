@@ -502,7 +502,8 @@ def run_long_context(a, dist: Dist, dev, pk) -> dict:
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_source": "measured bf16_tflops (burst)",
                          "frac_of_sustained": achieved / float(pk.get("bf16_tflops_sustained", peak)),
-                         "kernel": "fa_prefill_d256_kernel", "traffic": load_traffic("long_T%d" % T),
+                         "kernel": "fa_prefill_d256_kernel",
+                         "traffic": load_traffic("long_T%d" % T) if world == 1 else None,
                          "launch_ms": per_ms, "flops_per_launch": mine},
             "cpu_baseline": cpu}
 
