@@ -44,29 +44,13 @@ __device__ __forceinline__ PrefillItem<NQT> prefill_item(const PrefillParams& p,
   it.pairs = (NQT == 2 && p.head_pairs) ? 1 : 0;
   int qblk;
   if (it.pairs) {
-    // Items come in super blocks of two adjacent 128-row blocks, heaviest
-    // first; inside one, the 2 x np items of a KV head (both row blocks of
-    // every head pair) are adjacent, so the CTAs in flight at any time cover
-    // as few KV heads as in row mode (one 256-row block of every query head
-    // of the group) and their K/V stay in L2. With an odd number of row
-    // blocks the last super block holds row block 0 only.
+    // Heaviest row blocks first; the head pairs of one KV head adjacent.
     const int np = p.Hq / p.Hkv / 2;  // head pairs per KV head
     const int per = p.B * p.Hkv * np;
-    const int full = p.n_qblk / 2;    // super blocks with two row blocks
-    int pair, bk;
-    if (lin < full * 2 * per) {
-      const int g = lin / (2 * per);
-      const int rem = lin % (2 * per);
-      const int inner = rem % (2 * np);
-      bk = rem / (2 * np);
-      pair = inner % np;
-      qblk = p.n_qblk - 1 - (2 * g + inner / np);
-    } else {
-      const int rem = lin - full * 2 * per;
-      pair = rem % np;
-      bk = rem / np;
-      qblk = 0;
-    }
+    qblk = p.n_qblk - 1 - lin / per;
+    const int rem = lin % per;
+    const int pair = rem % np;
+    const int bk = rem / np;
     it.hk = bk % p.Hkv;
     it.b = bk / p.Hkv;
     it.h = it.hk * (2 * np) + 2 * pair;
@@ -640,10 +624,12 @@ static int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const 
 // kHeadPairMaxRows, two-tile items pair query heads when the GQA group size is
 // even: both tiles then walk the same key blocks, where row-pair items leave
 // tile 0 one block short on the diagonal, which at ~9 key blocks per item
-// (T = 2048) costs ~10 %. Measured on B200 (config 3 heads, TFLOP/s, head
-// pairs against row pairs, three passes): T=2048 853-893 against 784-826,
-// T=4096 982-992 against 1003-1038, T=8192 987-990 against 998-1002; at
-// T <= 1024 head-pair two-tile items were no faster than one-tile CTAs.
+// (T = 2048) costs ~10 %. Measured on B200 (config 3 heads, TFLOP/s, medians
+// of three alternating passes): T=2048 918 against 787 for row pairs, T=3072
+// 896 against 876; T=4096 and T=8192 ran 1-3 % slower with head pairs (more
+// KV heads in flight at once: their K/V no longer fit in L2, and ordering
+// items by KV head instead cost more at T=2048 than it saved there); at
+// T <= 1024 two-tile head-pair items were not faster than one-tile CTAs.
 PrefillPlan prefill_plan(int D, int Hq, int Hkv, int Tq, int Tk) {
   (void)D;
   (void)Tk;
