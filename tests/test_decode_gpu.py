@@ -151,3 +151,21 @@ def test_decode_proj_matches_decode_then_projection(cuda_dev, dtype, B, Hq, Hkv,
     ref_o = A.decode_ref(q.cpu(), kc.cpu(), vc.cpu(), lens)
     ref = x0.float().cpu() + ref_o.reshape(B, Hq * D) @ wo.float().cpu().T
     assert (x.float().cpu() - ref).abs().max().item() <= (TOL if dtype == torch.float32 else 6e-2) * scale
+
+
+@pytest.mark.parametrize("gate_dtype", [torch.float32, torch.bfloat16])
+def test_gated_decode_head_dim_128(cuda_dev, gate_dtype):
+    """b2a_decode_gated at D=128 (the gate fused into the combine kernel) with
+    a strided gate view, against the oracle times sigmoid(gate)."""
+    from npu_b200 import api
+
+    B, Hq, Hkv, D, Lmax = 3, 16, 2, 128, 900
+    lens = [1, 450, 900]
+    q, kc, vc, sl = _case(B, Hq, Hkv, Lmax, D, lens, 71, cuda_dev)
+    q, kc, vc, sl = q.to(cuda_dev), kc.to(cuda_dev), vc.to(cuda_dev), sl.to(cuda_dev)
+    gate_full = torch.randn(B, Hq, 2, D, generator=torch.Generator().manual_seed(72)).to(gate_dtype).to(cuda_dev)
+    gate = gate_full[:, :, 1]
+    out = api.decode(q, kc, vc, sl, gate=gate)
+    assert api.device_error() == 0
+    ref = A.decode_ref(q.cpu(), kc.cpu(), vc.cpu(), lens) * torch.sigmoid(gate.float().cpu())
+    assert (out.cpu() - ref).abs().max().item() <= TOL

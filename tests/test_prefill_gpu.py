@@ -372,3 +372,25 @@ def test_two_tile_items_head_pairs_and_row_pairs(cuda_dev, Hq, Hkv):
     s = (q.float().cpu() @ A.expand_kv(k.cpu().float(), Hq // Hkv).transpose(-1, -2)) / math.sqrt(D)
     s = s.masked_fill(A.causal_mask(Tq, Tk, sp), float("-inf"))
     assert (lse.cpu() - torch.logsumexp(s, dim=-1)).abs().max().item() < 1e-3
+
+
+@pytest.mark.parametrize("Tq,out_dtype,gate_dtype", [(300, torch.bfloat16, torch.bfloat16),
+                                                     (1300, torch.float32, torch.float32),
+                                                     (2100, torch.bfloat16, torch.float32)])
+def test_gated_prefill_head_dim_128(cuda_dev, Tq, out_dtype, gate_dtype):
+    """b2a_prefill_gated on the D <= 128 kernel (one-tile CTAs with the staged
+    bf16 store at Tq=300, head-pair items at 1300 and 2100): output =
+    attention * sigmoid(gate), the gate a strided view with a head stride of
+    2 D as in Qwen's [q_h | gate_h] projection."""
+    from npu_b200 import api
+
+    g = torch.Generator().manual_seed(Tq)
+    B, Hq, Hkv, D = 2, 8, 2, 128
+    Tk = Tq + 64
+    q, k, v = _rand((B, Hq, Tq, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev)
+    gate_full = torch.randn(B, Tq, Hq, 2, D, generator=g).to(gate_dtype).to(cuda_dev)
+    gate = gate_full[:, :, :, 1].transpose(1, 2)  # [B, Hq, Tq, D], strided
+    out = api.prefill(q, k, v, start_pos=64, gate=gate, out_dtype=out_dtype)
+    assert api.device_error() == 0
+    ref = A.dense_attention(q.cpu(), k.cpu(), v.cpu(), start_pos=64) * torch.sigmoid(gate.float().cpu())
+    assert (out.float().cpu() - ref).abs().max().item() <= TOL
