@@ -297,9 +297,13 @@ def run_ours(a, dist: Dist) -> dict | None:
         tot, per = timed(lambda: api.prefill(qs, ks, vs, scale=scale, out=os_, out_dtype=torch.bfloat16),
                          a.steps, a.warmup, dist)
         f = prefill_flops(B, Hq, D, Ts)
-        sweep.append({"T": Ts, "value": world * f * a.steps / (tot * 1e-3) / 1e12, "unit": "TFLOP/s",
-                      "ms_per_step": tot / a.steps, "scaling": "weak",
-                      "frac_of_peak": (f / (per * 1e-3) / 1e12) / peak})
+        entry = {"T": Ts, "value": world * f * a.steps / (tot * 1e-3) / 1e12, "unit": "TFLOP/s",
+                 "ms_per_step": tot / a.steps, "scaling": "weak",
+                 "frac_of_peak": (f / (per * 1e-3) / 1e12) / peak}
+        if rank == 0 and world == 1 and a.cpu_baseline:
+            # T=512: the whole batch (every (batch, KV head) unit); longer: a sample
+            entry["cpu_baseline"] = cpu_prefill_sample(Ts, B * Hkv if Ts <= 512 else a.cpu_units)
+        sweep.append(entry)
         del qs, ks, vs, os_
     torch.cuda.empty_cache()
 
