@@ -234,16 +234,12 @@ int prefill_impl(const void* q, const void* k, const void* v, void* o, float* ls
   const int kv_box = D == 256 ? 64 : 128;
   if ((rc = tmap_bf16_4d(&tk, k, D, Tk, kv_heads_map, B, ks[2], ks[1], ks[0], kv_box))) return rc;
   if ((rc = tmap_bf16_4d(&tv, v, D, Tk, kv_heads_map, B, vs[2], vs[1], vs[0], kv_box))) return rc;
-  // One-tile CTAs (two per SM) write bf16 output through a TMA store of each
-  // 128-row tile (box 64 columns x 128 rows): the store's reads of shared
-  // memory overlap the neighbouring CTA. Two-tile CTAs keep per-row stores,
-  // which let the CTA exit without waiting for a copy (measured: TMA store
-  // +3 % at T=512, -2 % at T=1024 there).
-  CUtensorMap to = tq;
-  const int o_tma = (!out_fp32 && plan.tiles == 1 && D != 256 &&
-                     tmap_bf16_4d(&to, o, D, Tq, Hq, B, os[2], os[1], os[0], 128) == B2A_OK)
-                        ? 1
-                        : 0;
+  // Per-row stores use 32-byte vector stores when O and its strides allow.
+  const int esz = out_fp32 ? 4 : 2;
+  const int o_v8 = (reinterpret_cast<uintptr_t>(o) % 32 == 0 && (os[0] * esz) % 32 == 0 &&
+                    (os[1] * esz) % 32 == 0 && (os[2] * esz) % 32 == 0)
+                       ? 1
+                       : 0;
 
   b2a::PrefillParams p{};
   p.o = o;
@@ -271,9 +267,9 @@ int prefill_impl(const void* q, const void* k, const void* v, void* o, float* ls
     p.g_st = gs[2];
     p.gate_bf16 = gate_bf16 ? 1 : 0;
   }
-  p.o_tma = o_tma;
+  p.o_v8 = o_v8;
   rc = D == 256 ? b2a::launch_prefill_d256(tq, tk, tv, p, static_cast<cudaStream_t>(stream))
-               : b2a::launch_prefill(D, plan, tq, tk, tv, to, p, static_cast<cudaStream_t>(stream));
+               : b2a::launch_prefill(D, plan, tq, tk, tv, p, static_cast<cudaStream_t>(stream));
   if (rc == -3) return B2A_ERR_HEAD_DIM;
   return rc ? B2A_ERR_LAUNCH : B2A_OK;
 }

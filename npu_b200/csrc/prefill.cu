@@ -82,8 +82,7 @@ __device__ __forceinline__ PrefillItem<NQT> prefill_item(const PrefillParams& p,
 template <int D, int NQT>
 __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT>::CTAS_PER_SM)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                      const __grid_constant__ PrefillParams p) {
+                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ PrefillParams p) {
   using C = PrefillCfg<D, NQT>;
   constexpr int kEmuPairs = exp2_emu_pairs<D>();
   // Warps that take every work item from the scheduler: the producer, the
@@ -119,10 +118,8 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
   const int first_loads = min(C::STAGES, 2 * first.n_kv);
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    // Every UMMA issuer commits once its last S MMA of an item is issued;
-    // with o_tma each tile's epilogue also arrives once its staged output has
-    // been read by the TMA store (the staging buffer is the Q buffer).
-    mbar_init(&bars->q_free, C::NQT * (p.o_tma ? 2 : 1));
+    // Every UMMA issuer commits once its last S MMA of an item is issued.
+    mbar_init(&bars->q_free, C::NQT);
 #pragma unroll
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&bars->kv_full[s], 1);
@@ -138,10 +135,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
       mbar_init(&bars->o_full[t], 1);
     }
 #pragma unroll
-    for (int t = 0; t < C::NQT; ++t) {
-      mbar_init(&bars->drain[t], 1);
-      mbar_init(&bars->staged[t], 4);
-    }
+    for (int t = 0; t < C::NQT; ++t) mbar_init(&bars->drain[t], 1);
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->item_full[s], 1);
@@ -209,7 +203,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
           issued = first_loads;
         } else {
           // The Q buffer is free once every S MMA of the previous item with
-          // keys has completed (and its staged output has been stored).
+          // keys has completed.
           if (!wait_all(&bars->q_free, (uint32_t)(q_rounds - 1) & 1u)) {
             ok = false;
             break;
@@ -437,7 +431,6 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
     int J = 0;         // key blocks of this tile in earlier items (barrier rounds)
     int o_rounds = 0;  // earlier items in which this tile had key blocks
     bool ok = true;
-    const uint32_t stage = smem_u32(sQ + t * C::Q_TILE_BYTES);
     for (int n = 1;; ++n) {
       const PrefillItem<NQT> it = prefill_item<NQT>(p, lin);
       const int b = it.b, h = it.head(t);
@@ -534,28 +527,20 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
         }
       } else {
         const bool w = ok && mbar_wait(&bars->o_full[t], (uint32_t)o_rounds & 1u, abort_flag, p.err);
-        // With o_tma the tile's rows are staged in its Q buffer, which no MMA
-        // reads any more (all of tile t's S MMAs completed before o_full[t]),
-        // and written out by one TMA store; rows past Tq are clipped by it.
         if (__all_sync(0xffffffffu, w)) {
           tc_fence_after();
           const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+          // Two 32-column TMEM loads per wait: the second load's latency
+          // hides behind the first.
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + 32 * c, o);
+          for (int c = 0; c < D / 32; c += 2) {
+            uint32_t o[2][32];
+            tmem_ld32(tO + 32 * c, o[0]);
+            tmem_ld32(tO + 32 * c + 32, o[1]);
             tmem_wait_ld();
-            if (p.o_tma) {
-              float v[32];
-              if (valid) {
-                out_chunk_values(p, b, h, grow, c, o, inv_l, v);
-              } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = 0.f;
-              }
-              stage_out_chunk_bf16(stage, C::CHUNK_BYTES, row, c, v);
-            } else if (valid) {
-              store_out_chunk(p, b, h, grow, c, o, inv_l);
+            if (valid) {
+              store_out_chunk(p, b, h, grow, c, o[0], inv_l);
+              store_out_chunk(p, b, h, grow, c + 1, o[1], inv_l);
             }
           }
           if (p.lse && valid) {
@@ -563,26 +548,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
                 l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994531f : -INFINITY;
           }
         }
-        if (p.o_tma) {
-          // Each of the tile's four warps reports its staged rows (also on
-          // the abort path); row 0 waits for all four with a bounded wait and
-          // issues the store. The round is this tile's o_rounds.
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bars->staged[t]);
-          if (row == 0 && mbar_wait(&bars->staged[t], (uint32_t)o_rounds & 1u, abort_flag, p.err) &&
-              !*abort_flag) {
-#pragma unroll
-            for (int c = 0; c < C::KCH; ++c)
-              tma_store_4d(&tm_o, sQ + t * C::Q_TILE_BYTES + c * C::CHUNK_BYTES, c * 64, it.row0(t), h, b);
-            tma_store_commit();
-            tma_store_wait_read();  // the staging buffer must outlive the copy's reads
-          }
-        }
       }
-      // With o_tma the Q buffer is also this tile's output staging: the next
-      // item's Q may only land once the store above has read it.
-      if (p.o_tma && it.n_kv > 0 && row == 0) mbar_arrive(&bars->q_free);
       J += n_mine;
       if (n_mine > 0) ++o_rounds;
       if (!ok) break;
@@ -603,7 +569,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
 // ------------------------------------------------------------------ launcher
 template <int D, int NQT>
 static int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                            const CUtensorMap& to, const PrefillParams& p, cudaStream_t st) {
+                            const PrefillParams& p, cudaStream_t st) {
   using C = PrefillCfg<D, NQT>;
   cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<D, NQT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM_BYTES);
@@ -615,7 +581,7 @@ static int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const 
   // One CTA per work item (query blocks x query heads, or x head pairs).
   const long long nblk = (long long)p.n_qblk * p.B * (p.head_pairs ? p.Hq / 2 : p.Hq);
   if (nblk <= 0 || nblk > 0x7fffffffLL) return -2;
-  fa_prefill_kernel<D, NQT><<<(unsigned)nblk, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, to, p);
+  fa_prefill_kernel<D, NQT><<<(unsigned)nblk, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -640,14 +606,14 @@ PrefillPlan prefill_plan(int D, int Hq, int Hkv, int Tq, int Tk) {
 }
 
 int launch_prefill(int D, const PrefillPlan& plan, const CUtensorMap& tq, const CUtensorMap& tk,
-                   const CUtensorMap& tv, const CUtensorMap& to, const PrefillParams& p, cudaStream_t st) {
+                   const CUtensorMap& tv, const PrefillParams& p, cudaStream_t st) {
   const bool one = plan.tiles == 1;
   switch (D) {
     case 64:
-      return one ? launch_prefill_t<64, 1>(tq, tk, tv, to, p, st) : launch_prefill_t<64, 2>(tq, tk, tv, to, p, st);
+      return one ? launch_prefill_t<64, 1>(tq, tk, tv, p, st) : launch_prefill_t<64, 2>(tq, tk, tv, p, st);
     case 128:
-      return one ? launch_prefill_t<128, 1>(tq, tk, tv, to, p, st)
-                 : launch_prefill_t<128, 2>(tq, tk, tv, to, p, st);
+      return one ? launch_prefill_t<128, 1>(tq, tk, tv, p, st)
+                 : launch_prefill_t<128, 2>(tq, tk, tv, p, st);
     default: return -3;
   }
 }

@@ -74,10 +74,9 @@ struct PrefillParams {
   const void* gate;
   long long g_sb, g_sh, g_st;
   int gate_bf16;
-  // 1: O is bf16 and the kernel's O tensor map is valid, so each tile's
-  // output goes through shared memory (the tile's spent Q buffer) and one
-  // TMA store instead of per-row global stores.
-  int o_tma;
+  // 1: O's base and strides are 32-byte aligned, so the epilogue's
+  // row-per-thread stores may be 32-byte vector stores.
+  int o_v8;
 };
 
 // NQT query tiles of 128 rows per CTA. NQT = 2: the two tiles' softmax and
@@ -126,7 +125,6 @@ struct PrefillBars {
   uint64_t q_full;
   uint64_t q_free;       // the Q buffer may be refilled for the next work
                          // item: every S MMA of the current one has completed
-                         // (and, with o_tma, its output staged there is stored)
   uint64_t kv_full[8];
   uint64_t kv_empty[8];
   uint64_t sa_full[2];   // first 64-key half of S_t(j) is in TMEM
@@ -137,8 +135,6 @@ struct PrefillBars {
   uint64_t p_full[2];
   uint64_t o_full[2];
   uint64_t drain[2];     // per UMMA issuer warp
-  uint64_t staged[2];    // o_tma: the tile's four softmax warps have staged
-                         // their output rows (one arrive per warp)
   // Work items beyond the CTA's own are taken from CTAs of the grid that have
   // not started yet (cluster launch control); the scheduler warp publishes
   // each one in a two-slot ring read by every other warp.
@@ -169,9 +165,7 @@ PrefillPlan prefill_plan(int D, int Hq, int Hkv, int Tq, int Tk);
 // Launch the prefill kernel on `st` for the given plan.
 // Returns 0 on success, -3 for an unsupported head_dim, another negative
 // value on launch failure.
-// `to` describes O (4-D, 64-column x 128-row boxes, 128-byte swizzle) when
-// p.o_tma is set; it is not read otherwise.
 int launch_prefill(int D, const PrefillPlan& plan, const CUtensorMap& tq, const CUtensorMap& tk,
-                   const CUtensorMap& tv, const CUtensorMap& to, const PrefillParams& p, cudaStream_t st);
+                   const CUtensorMap& tv, const PrefillParams& p, cudaStream_t st);
 
 }  // namespace b2a

@@ -310,13 +310,31 @@ __device__ __forceinline__ void out_chunk_values(const PrefillParams& p, int b, 
 }
 
 // Scale one 32-column chunk of an output row (out_chunk_values) and store it
-// (fp32 or bf16) with 16-byte stores.
+// (fp32 or bf16) with 32-byte stores where O is aligned for them (p.o_v8: a
+// warp's row-per-thread stores then write whole 32-byte sectors, with half
+// the store instructions), else 16-byte stores.
 __device__ __forceinline__ void store_out_chunk(const PrefillParams& p, int b, int h, int grow, int c,
                                                 const uint32_t (&o)[32], float inv_l) {
   float v[32];
   out_chunk_values(p, b, h, grow, c, o, inv_l, v);
   const long long base = (long long)b * p.o_sb + (long long)h * p.o_sh + (long long)grow * p.o_st + 32 * c;
-  if (p.out_fp32) {
+  if (p.o_v8) {
+    if (p.out_fp32) {
+      float* dst = reinterpret_cast<float*>(p.o) + base;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        st_global_v8(dst + 8 * i, f2u(v[8 * i]), f2u(v[8 * i + 1]), f2u(v[8 * i + 2]), f2u(v[8 * i + 3]),
+                     f2u(v[8 * i + 4]), f2u(v[8 * i + 5]), f2u(v[8 * i + 6]), f2u(v[8 * i + 7]));
+    } else {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.o) + base;
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+        st_global_v8(dst + 16 * i, pack_bf16x2(v[16 * i], v[16 * i + 1]), pack_bf16x2(v[16 * i + 2], v[16 * i + 3]),
+                     pack_bf16x2(v[16 * i + 4], v[16 * i + 5]), pack_bf16x2(v[16 * i + 6], v[16 * i + 7]),
+                     pack_bf16x2(v[16 * i + 8], v[16 * i + 9]), pack_bf16x2(v[16 * i + 10], v[16 * i + 11]),
+                     pack_bf16x2(v[16 * i + 12], v[16 * i + 13]), pack_bf16x2(v[16 * i + 14], v[16 * i + 15]));
+    }
+  } else if (p.out_fp32) {
     float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.o) + base);
 #pragma unroll
     for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
@@ -331,22 +349,6 @@ __device__ __forceinline__ void store_out_chunk(const PrefillParams& p, int b, i
       w.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
       dst[i] = w;
     }
-  }
-}
-
-// Write one 32-column chunk (bf16) of an output row into a 128-row tile in
-// shared memory laid out as a TMA SWIZZLE_128B box of 64 columns: chunk c of
-// row r goes to 64-column block c / 2, 16-byte units (c % 2) * 4 .. + 3, each
-// unit index XORed with (r & 7). The tile is then stored with tma_store_4d.
-__device__ __forceinline__ void stage_out_chunk_bf16(uint32_t tile, int block_bytes, int r, int c,
-                                                     const float (&v)[32]) {
-  const uint32_t base = tile + (c >> 1) * block_bytes + r * 128;
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int unit = (c & 1) * 4 + u;
-    st_shared_v4(base + ((unit ^ (r & 7)) << 4), pack_bf16x2(v[8 * u], v[8 * u + 1]),
-                 pack_bf16x2(v[8 * u + 2], v[8 * u + 3]), pack_bf16x2(v[8 * u + 4], v[8 * u + 5]),
-                 pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
   }
 }
 

@@ -127,8 +127,9 @@ def test_strided_bthd_inputs(cuda_dev):
 @pytest.mark.parametrize("D", [64, 128])
 def test_bf16_output_into_strided_bthd_buffer(cuda_dev, D):
     """bf16 output written into a [B, T, H, D] buffer viewed as [B, H, T, D]
-    (the layout the output projection reads), with a ragged T: the tile store
-    must clip the rows past T and leave the rest of the buffer untouched."""
+    (the layout the output projection reads), with a ragged T: the rows past T
+    of the last query block must not be written, the rest of the buffer stays
+    untouched."""
     from npu_b200 import api
 
     g = torch.Generator().manual_seed(15 + D)
@@ -140,6 +141,29 @@ def test_bf16_output_into_strided_bthd_buffer(cuda_dev, D):
     ref = A.dense_attention(q.cpu(), k.cpu(), v.cpu())
     assert (out.float().cpu() - ref).abs().max().item() <= TOL
     assert torch.all(buf[:, T:] == 7.0)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("T", [300, 1100])
+def test_output_16_byte_aligned_only(cuda_dev, out_dtype, T):
+    """An output 16 bytes past a 32-byte boundary takes the 16-byte store path
+    (the 32-byte vector stores need 32-byte alignment); one-tile (T=300) and
+    two-tile (T=1100) work items. The words around the output stay as they
+    were."""
+    from npu_b200 import api
+
+    g = torch.Generator().manual_seed(77 + T)
+    B, Hq, Hkv, D = 1, 4, 2, 128
+    q, k, v = _rand((B, Hq, T, D), g, cuda_dev), _rand((B, Hkv, T, D), g, cuda_dev), _rand((B, Hkv, T, D), g, cuda_dev)
+    n = B * Hq * T * D
+    pad = 16 // torch.tensor([], dtype=out_dtype).element_size()
+    flat = torch.full((n + 2 * pad,), 3.0, dtype=out_dtype, device=cuda_dev)
+    assert flat.data_ptr() % 32 == 0
+    out = flat[pad:pad + n].view(B, Hq, T, D)
+    api.prefill(q, k, v, out_dtype=out_dtype, out=out)
+    ref = A.dense_attention(q.cpu(), k.cpu(), v.cpu())
+    assert (out.float().cpu() - ref).abs().max().item() <= TOL
+    assert torch.all(flat[:pad] == 3.0) and torch.all(flat[pad + n:] == 3.0)
 
 
 def test_fully_masked_rows_and_empty_keys(cuda_dev):
