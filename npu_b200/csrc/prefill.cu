@@ -18,6 +18,9 @@ constexpr int kOneTileMaxRows = B2A_ONE_TILE_MAX_ROWS;
 // query is at most this long; longer queries use row-pair items.
 constexpr bool kHeadPairs = B2A_HEAD_PAIRS != 0;
 constexpr int kHeadPairMaxRows = 3072;
+// With an even GQA group, queries longer than this use head-pair items
+// instead of one-tile CTAs.
+constexpr int kHeadPairMinRows = 513;
 
 
 // Work item -> (query block, batch, heads) and the key blocks its query tiles
@@ -586,22 +589,25 @@ static int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const 
 }
 
 // One-tile CTAs (two per SM) pay off when a CTA sees few key blocks, so that
-// its start-up and epilogue are a large share of its time. Between that and
+// its start-up and epilogue are a large share of its time. Beyond that, up to
 // kHeadPairMaxRows, two-tile items pair query heads when the GQA group size is
-// even: both tiles then walk the same key blocks, where row-pair items leave
-// tile 0 one block short on the diagonal, which at ~9 key blocks per item
-// (T = 2048) costs ~10 %. Measured on B200 (config 3 heads, TFLOP/s, medians
-// of three alternating passes): T=2048 918 against 787 for row pairs, T=3072
-// 896 against 876; T=4096 and T=8192 ran 1-3 % slower with head pairs (more
-// KV heads in flight at once: their K/V no longer fit in L2, and ordering
-// items by KV head instead cost more at T=2048 than it saved there); at
-// T <= 1024 two-tile head-pair items were not faster than one-tile CTAs.
+// even: both tiles then walk the same key blocks (row-pair items leave tile 0
+// one block short on the diagonal, ~10 % at T = 2048), and one K/V stream
+// feeds two tiles through the 5-slot ring, where a one-tile CTA's 2-slot ring
+// leaves each block's loads exposed. Measured on B200 (config 3 heads,
+// TFLOP/s, interleaved A/B, medians): one-tile CTAs against head pairs
+// T=256 347 / 323, T=512 547 / 551, T=768 657 / 697, T=1024 696 / 744;
+// head pairs against row pairs T=2048 918 / 787, T=3072 896 / 876; at T=4096
+// and 8192 head pairs ran 1-3 % slower (more KV heads in flight at once:
+// their K/V no longer fit in L2). Odd groups keep one-tile CTAs up to
+// kOneTileMaxRows (measured against row pairs: T=1024 +2-3 %, T=2048 -10 %).
 PrefillPlan prefill_plan(int D, int Hq, int Hkv, int Tq, int Tk) {
   (void)D;
   (void)Tk;
-  if (Tq <= kOneTileMaxRows) return PrefillPlan{128, 1, 0};
   const bool even_group = Hkv > 0 && Hq % Hkv == 0 && (Hq / Hkv) % 2 == 0;
-  if (kHeadPairs && even_group && Tq <= kHeadPairMaxRows) return PrefillPlan{128, 2, 1};
+  if (kHeadPairs && even_group && Tq >= kHeadPairMinRows && Tq <= kHeadPairMaxRows)
+    return PrefillPlan{128, 2, 1};
+  if (Tq <= kOneTileMaxRows) return PrefillPlan{128, 1, 0};
   return PrefillPlan{256, 2, 0};
 }
 

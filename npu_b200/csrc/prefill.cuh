@@ -11,7 +11,7 @@
 //
 // A work item is two 128-row query tiles that ping-pong on the tensor core,
 // so one tile's softmax overlaps the other tile's MMAs: a 256-row query block
-// of one (batch, query head), or, for queries of 1025-3072 rows with an even
+// of one (batch, query head), or, for queries of 513-3072 rows with an even
 // GQA group, the same 128 rows of two query heads that share a KV head (both
 // tiles then walk the same key blocks). The grid has one CTA per work item, but a CTA does not
 // stop after its own: it takes over CTAs that have not started yet (cluster

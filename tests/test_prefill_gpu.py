@@ -377,17 +377,19 @@ def test_config5_full_length_sampled_rows(cuda_dev):
     assert not torch.isnan(out).any()
 
 
+@pytest.mark.parametrize("Tq", [600, 1300])
 @pytest.mark.parametrize("Hq,Hkv", [(8, 2), (6, 2), (16, 16)])
-def test_two_tile_items_head_pairs_and_row_pairs(cuda_dev, Hq, Hkv):
-    """Queries longer than 1024 rows run as two-tile work items: two query
-    heads of one KV head over the same 128 rows when the GQA group is even
-    (8/2), else two 128-row blocks of one head (6/2 with group 3; 16/16 with
-    group 1). Ragged query length, a chunked start and the LSE, all rows
-    against the oracle."""
+def test_two_tile_items_head_pairs_and_row_pairs(cuda_dev, Hq, Hkv, Tq):
+    """Work items by query length and GQA group: with an even group (8/2)
+    queries of 513-3072 rows run as two query heads of one KV head over the
+    same 128 rows (Tq 600 and 1300); odd groups (6/2 with group 3; 16/16 with
+    group 1) run one-tile CTAs up to 1024 rows (Tq 600) and two 128-row
+    blocks of one head beyond (Tq 1300). Ragged query length, a chunked start
+    and the LSE, all rows against the oracle."""
     from npu_b200 import api
 
-    g = torch.Generator().manual_seed(40 + Hq)
-    B, Tq, Tk, D, sp = 2, 1300, 1500, 128, 200
+    g = torch.Generator().manual_seed(40 + Hq + Tq)
+    B, Tk, D, sp = 2, Tq + 200, 128, 200
     q, k, v = _rand((B, Hq, Tq, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev), _rand((B, Hkv, Tk, D), g, cuda_dev)
     out, lse = api.prefill(q, k, v, start_pos=sp, return_lse=True)
     assert api.device_error() == 0
@@ -402,8 +404,8 @@ def test_two_tile_items_head_pairs_and_row_pairs(cuda_dev, Hq, Hkv):
                                                      (1300, torch.float32, torch.float32),
                                                      (2100, torch.bfloat16, torch.float32)])
 def test_gated_prefill_head_dim_128(cuda_dev, Tq, out_dtype, gate_dtype):
-    """b2a_prefill_gated on the D <= 128 kernel (one-tile CTAs with the staged
-    bf16 store at Tq=300, head-pair items at 1300 and 2100): output =
+    """b2a_prefill_gated on the D <= 128 kernel (one-tile CTAs at Tq=300,
+    head-pair items at 1300 and 2100): output =
     attention * sigmoid(gate), the gate a strided view with a head stride of
     2 D as in Qwen's [q_h | gate_h] projection."""
     from npu_b200 import api
