@@ -29,24 +29,23 @@ constexpr int kHeadPairMinRows = 513;
 // re-read K/V from L2. Row mode: tile t covers rows [q0 + 128 t, +128) of
 // query head h. Head-pair mode (NQT = 2, head_pairs): tile t covers rows
 // [q0, q0 + 128) of query head h + t.
-template <int NQT>
+template <int NQT, bool PAIRS>
 struct PrefillItem {
+  static_assert(!PAIRS || NQT == 2, "head-pair items have two tiles");
   int h, b, hk, q0, sp;
-  int pairs;     // 1: head-pair item
   int n_t[NQT];  // key blocks query tile t needs; tile 0 never more than
                  // tile 1 and, under the causal mask, at most one fewer
   int n_kv;      // n_t[NQT - 1]: the key blocks that get loaded
-  __device__ __forceinline__ int head(int t) const { return h + (pairs ? t : 0); }
-  __device__ __forceinline__ int row0(int t) const { return q0 + (pairs ? 0 : 128 * t); }
+  __device__ __forceinline__ int head(int t) const { return h + (PAIRS ? t : 0); }
+  __device__ __forceinline__ int row0(int t) const { return q0 + (PAIRS ? 0 : 128 * t); }
 };
 
-template <int NQT>
-__device__ __forceinline__ PrefillItem<NQT> prefill_item(const PrefillParams& p, int lin) {
+template <int NQT, bool PAIRS>
+__device__ __forceinline__ PrefillItem<NQT, PAIRS> prefill_item(const PrefillParams& p, int lin) {
   constexpr int BM = 128, BN = 128;
-  PrefillItem<NQT> it;
-  it.pairs = (NQT == 2 && p.head_pairs) ? 1 : 0;
+  PrefillItem<NQT, PAIRS> it;
   int qblk;
-  if (it.pairs) {
+  if (PAIRS) {
     // Heaviest row blocks first; the head pairs of one KV head adjacent.
     const int np = p.Hq / p.Hkv / 2;  // head pairs per KV head
     const int per = p.B * p.Hkv * np;
@@ -82,7 +81,8 @@ __device__ __forceinline__ PrefillItem<NQT> prefill_item(const PrefillParams& p,
   return it;
 }
 
-template <int D, int NQT>
+// PAIRS: head-pair work items (NQT = 2 only), else row blocks.
+template <int D, int NQT, bool PAIRS>
 __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT>::CTAS_PER_SM)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ PrefillParams p) {
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
     return id;
   };
 
-  const PrefillItem<NQT> first = prefill_item<NQT>(p, blockIdx.x);
+  const PrefillItem<NQT, PAIRS> first = prefill_item<NQT, PAIRS>(p, blockIdx.x);
   const int first_loads = min(C::STAGES, 2 * first.n_kv);
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
@@ -139,6 +139,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
     }
 #pragma unroll
     for (int t = 0; t < C::NQT; ++t) mbar_init(&bars->drain[t], 1);
+    mbar_init(&bars->stagger, 4);
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->item_full[s], 1);
@@ -198,7 +199,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
     int q_rounds = 0;  // items with keys (one Q load each)
     bool ok = true;
     for (int n = 1;; ++n) {
-      const PrefillItem<NQT> it = prefill_item<NQT>(p, lin);
+      const PrefillItem<NQT, PAIRS> it = prefill_item<NQT, PAIRS>(p, lin);
       if (it.n_kv > 0) {
         int i0 = 0;
         if (n == 1) {
@@ -292,9 +293,10 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
     int G = 0;         // ring position of the current item's first load
     int J = 0;         // key blocks of this tile in earlier items (barrier rounds)
     int q_rounds = 0;  // items with keys so far
+    int stg = 0;       // head-pair items with keys so far (stagger rounds)
     bool ok = true;
     for (int n = 1;; ++n) {
-      const PrefillItem<NQT> it = prefill_item<NQT>(p, lin);
+      const PrefillItem<NQT, PAIRS> it = prefill_item<NQT, PAIRS>(p, lin);
       const int nt = t == 0 ? it.n_t[0] : it.n_kv;
       if (it.n_kv > 0) {
         auto slot_of = [&](int i) { return (G + i) % C::STAGES; };
@@ -314,6 +316,18 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
         // the first PV (the one that overwrites O) waits for.
         ok = wait_all(&bars->q_full, (uint32_t)q_rounds & 1u);
         ++q_rounds;
+        // Head-pair items: tile 1 starts one block behind tile 0 (its first S
+        // MMAs wait for tile 0's first mid), so the two tiles' epilogues,
+        // whose row stores would otherwise hit the memory pipe at the same
+        // moment, fall into the other tile's key loop (row-pair items are
+        // offset by the diagonal block already). Measured +5 % at T = 1024,
+        // +2.5 % at T = 2048. Tile 0 cannot publish the next item's first mid
+        // before this wait has passed: that needs the next Q, which needs
+        // q_free, which needs this warp's S MMAs of this item.
+        if (PAIRS && t == 1 && it.n_t[0] > 0) {
+          ok = ok && wait_all(&bars->stagger, (uint32_t)stg & 1u);
+          ++stg;
+        }
         int used = 0;
         if (ok && nt > 0) {
           ok = wait_load(0);
@@ -435,7 +449,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
     int o_rounds = 0;  // earlier items in which this tile had key blocks
     bool ok = true;
     for (int n = 1;; ++n) {
-      const PrefillItem<NQT> it = prefill_item<NQT>(p, lin);
+      const PrefillItem<NQT, PAIRS> it = prefill_item<NQT, PAIRS>(p, lin);
       const int b = it.b, h = it.head(t);
       const int grow = it.row0(t) + row;
       const bool valid = grow < p.Tq;
@@ -497,6 +511,7 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->mid[t]);
+        if (PAIRS && t == 0 && j == 0 && lane == 0) mbar_arrive(&bars->stagger);
         const float a1 = softmax_half_tmem<kEmuPairs>(s, lim - C::HALF, sl2, m_run, tR + fcol + 32, hs1);
         if (__any_sync(0xffffffffu, a1 != 1.f)) {
           // Rare: the second half moved the running max. O then holds blocks
@@ -570,21 +585,21 @@ __global__ void __launch_bounds__(PrefillCfg<D, NQT>::THREADS, PrefillCfg<D, NQT
 }
 
 // ------------------------------------------------------------------ launcher
-template <int D, int NQT>
+template <int D, int NQT, bool PAIRS>
 static int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                             const PrefillParams& p, cudaStream_t st) {
   using C = PrefillCfg<D, NQT>;
-  cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<D, NQT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<D, NQT, PAIRS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM_BYTES);
   if (e != cudaSuccess) return -1;
   // The in-kernel register split needs at least MIN_LAUNCH_REGS per thread.
   cudaFuncAttributes fa{};
-  if (cudaFuncGetAttributes(&fa, fa_prefill_kernel<D, NQT>) != cudaSuccess || fa.numRegs < C::MIN_LAUNCH_REGS)
+  if (cudaFuncGetAttributes(&fa, fa_prefill_kernel<D, NQT, PAIRS>) != cudaSuccess || fa.numRegs < C::MIN_LAUNCH_REGS)
     return -1;
   // One CTA per work item (query blocks x query heads, or x head pairs).
   const long long nblk = (long long)p.n_qblk * p.B * (p.head_pairs ? p.Hq / 2 : p.Hq);
   if (nblk <= 0 || nblk > 0x7fffffffLL) return -2;
-  fa_prefill_kernel<D, NQT><<<(unsigned)nblk, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, p);
+  fa_prefill_kernel<D, NQT, PAIRS><<<(unsigned)nblk, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -614,12 +629,16 @@ PrefillPlan prefill_plan(int D, int Hq, int Hkv, int Tq, int Tk) {
 int launch_prefill(int D, const PrefillPlan& plan, const CUtensorMap& tq, const CUtensorMap& tk,
                    const CUtensorMap& tv, const PrefillParams& p, cudaStream_t st) {
   const bool one = plan.tiles == 1;
+  const bool pairs = !one && plan.head_pairs;
   switch (D) {
     case 64:
-      return one ? launch_prefill_t<64, 1>(tq, tk, tv, p, st) : launch_prefill_t<64, 2>(tq, tk, tv, p, st);
+      return one ? launch_prefill_t<64, 1, false>(tq, tk, tv, p, st)
+                 : (pairs ? launch_prefill_t<64, 2, true>(tq, tk, tv, p, st)
+                          : launch_prefill_t<64, 2, false>(tq, tk, tv, p, st));
     case 128:
-      return one ? launch_prefill_t<128, 1>(tq, tk, tv, p, st)
-                 : launch_prefill_t<128, 2>(tq, tk, tv, p, st);
+      return one ? launch_prefill_t<128, 1, false>(tq, tk, tv, p, st)
+                 : (pairs ? launch_prefill_t<128, 2, true>(tq, tk, tv, p, st)
+                          : launch_prefill_t<128, 2, false>(tq, tk, tv, p, st));
     default: return -3;
   }
 }

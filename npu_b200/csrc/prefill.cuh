@@ -135,6 +135,8 @@ struct PrefillBars {
   uint64_t p_full[2];
   uint64_t o_full[2];
   uint64_t drain[2];     // per UMMA issuer warp
+  uint64_t stagger;      // head-pair items: tile 0's softmax warps have
+                         // published the item's first mid
   // Work items beyond the CTA's own are taken from CTAs of the grid that have
   // not started yet (cluster launch control); the scheduler warp publishes
   // each one in a two-slot ring read by every other warp.
