@@ -333,7 +333,7 @@ def run_ours(a, dist: Dist) -> dict | None:
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_source": f"{pk_src} bf16_tflops (burst)",
                      "frac_of_sustained": achieved / float(pk.get("bf16_tflops_sustained", peak)),
-                     "kernel": "fa_prefill_kernel<128>", "traffic": traffic,
+                     "kernel": "fa_prefill_kernel<128, 2, false>", "traffic": traffic,
                      "flops_per_launch": flops_rank, "launch_ms": per_ms},
         "e2e": e2e,
         "gpu_launches": a.steps,
