@@ -84,6 +84,15 @@ bool make_plan(int B, int Hq, int Hkv, int Tq, int Tk, int D, int out_fp32, int 
   if (per >= Hkv) {
     const int nb = (int)((per + Hkv - 1) / Hkv);
     for (int b = 0; b < B; b += nb) pl->chunks.push_back({b, nb < B - b ? nb : B - b, 0, Hkv});
+    // Taper: the last chunk's kernel and download run after every upload is
+    // done, with nothing left to overlap them. Split its last batch into one
+    // chunk per KV head, so only a small piece remains in that tail.
+    if (pl->chunks.size() > 1 && Hkv > 1) {
+      Chunk& last = pl->chunks.back();
+      const int bl = last.b0 + last.nb - 1;
+      if (--last.nb == 0) pl->chunks.pop_back();
+      for (int h = 0; h < Hkv; ++h) pl->chunks.push_back({bl, 1, h, 1});
+    }
   } else {
     const int nh = (int)per;
     for (int b = 0; b < B; ++b)
@@ -143,8 +152,8 @@ int b2a_prefill_host(const void* q, const void* k, const void* v, void* o, int B
 
   bool ok = cudaEventRecord(e->fork, st) == cudaSuccess && cudaStreamWaitEvent(e->up, e->fork, 0) == cudaSuccess &&
             cudaStreamWaitEvent(e->down, e->fork, 0) == cudaSuccess;
-  const bool whole_batches = pl.chunks[0].nh == Hkv;
-  if (ok && start_pos_per_batch && whole_batches)
+  const bool any_whole = pl.chunks[0].nh == Hkv;  // whole-batch chunks come first
+  if (ok && start_pos_per_batch && any_whole)
     ok = cudaMemcpyAsync(pos_dev, start_pos_per_batch, (size_t)B * sizeof(int), cudaMemcpyHostToDevice, e->up) ==
          cudaSuccess;
 
@@ -189,7 +198,7 @@ int b2a_prefill_host(const void* q, const void* k, const void* v, void* o, int B
     int sp = start_pos;
     const int* sp_arr = nullptr;
     if (start_pos_per_batch) {
-      if (whole_batches)
+      if (c.nh == Hkv)
         sp_arr = pos_dev + c.b0;
       else
         sp = start_pos_per_batch[c.b0];
