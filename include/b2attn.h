@@ -83,6 +83,11 @@ B2A_API int b2a_version(void);
  * reference, npu/fa_ref.py:68). Tk may be 0: every row is then 0 and k / v
  * are not read (they may be NULL).
  * Supported D: 64, 128, 256.
+ * With the environment variable B2A_PREFILL_SM_PAIRS set to a positive row
+ * count, head dim 128 queries with an even GQA group and at least that many
+ * rows run on SM pairs (a two-CTA cluster per 256 rows of two query heads,
+ * tcgen05.mma.cta_group::2): same results bit for bit, measured slower than
+ * the default one-SM kernel, so off unless asked for. Read on every call.
  */
 B2A_API int b2a_prefill(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv,
                 int Tq, int Tk, int D, const long long* q_strides, const long long* k_strides,

@@ -23,8 +23,8 @@ INCLUDE = ROOT / "include"
 LIB = PKG / "libb2attn.so"
 BUILD_DIR = PKG / "_build"
 
-SOURCES = ["capi.cu", "prefill.cu", "prefill_d256.cu", "decode.cu", "decode_noalloc.cu", "rope_append.cu", "diag.cu",
-           "host_pipeline.cu"]
+SOURCES = ["capi.cu", "prefill.cu", "prefill_pair.cu", "prefill_d256.cu", "decode.cu", "decode_noalloc.cu",
+           "rope_append.cu", "diag.cu", "host_pipeline.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3", "-std=c++17", "-lineinfo", "--use_fast_math",

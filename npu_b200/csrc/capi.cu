@@ -218,7 +218,7 @@ int prefill_impl(const void* q, const void* k, const void* v, void* o, float* ls
   // Work items: 128 query rows for D = 256; for D <= 128 two 128-row tiles
   // (two row blocks of one head, or one row block of two heads of a GQA
   // group), or one tile for short sequences (prefill_plan).
-  const b2a::PrefillPlan plan = D == 256 ? b2a::PrefillPlan{128, 1, 0} : b2a::prefill_plan(D, Hq, Hkv, Tq, Tk);
+  const b2a::PrefillPlan plan = D == 256 ? b2a::PrefillPlan{128, 1, 0, 0} : b2a::prefill_plan(D, Hq, Hkv, Tq, Tk);
   const int rows_per_cta = plan.rows_per_item;
   const long long n_qblk = (Tq + rows_per_cta - 1) / rows_per_cta;
   if (n_qblk * Hq * (long long)B > 0x7fffffffLL) return B2A_ERR_INVALID_ARG;
@@ -230,9 +230,11 @@ int prefill_impl(const void* q, const void* k, const void* v, void* o, float* ls
   CUtensorMap tq, tk, tv;
   if ((rc = tmap_bf16_4d(&tq, q, D, Tq, Hq, B, qs[2], qs[1], qs[0], 128))) return rc;
   const int kv_heads_map = Tk == 0 ? Hq : Hkv;  // Tk == 0: maps describe q, never loaded
-  // Key-tile rows per TMA box: 128 for the two-tile kernel, 64 for D = 256.
+  // Key-tile rows per TMA box: 128 for the two-tile kernel, 64 for D = 256;
+  // on SM pairs each CTA loads 32-key pieces of K and 128-key halves of V.
   const int kv_box = D == 256 ? 64 : 128;
-  if ((rc = tmap_bf16_4d(&tk, k, D, Tk, kv_heads_map, B, ks[2], ks[1], ks[0], kv_box))) return rc;
+  const int k_box = plan.sm_pairs ? 32 : kv_box;
+  if ((rc = tmap_bf16_4d(&tk, k, D, Tk, kv_heads_map, B, ks[2], ks[1], ks[0], k_box))) return rc;
   if ((rc = tmap_bf16_4d(&tv, v, D, Tk, kv_heads_map, B, vs[2], vs[1], vs[0], kv_box))) return rc;
   // Per-row stores use 32-byte vector stores when O and its strides allow.
   const int esz = out_fp32 ? 4 : 2;
@@ -268,8 +270,9 @@ int prefill_impl(const void* q, const void* k, const void* v, void* o, float* ls
     p.gate_bf16 = gate_bf16 ? 1 : 0;
   }
   p.o_v8 = o_v8;
-  rc = D == 256 ? b2a::launch_prefill_d256(tq, tk, tv, p, static_cast<cudaStream_t>(stream))
-               : b2a::launch_prefill(D, plan, tq, tk, tv, p, static_cast<cudaStream_t>(stream));
+  rc = D == 256        ? b2a::launch_prefill_d256(tq, tk, tv, p, static_cast<cudaStream_t>(stream))
+       : plan.sm_pairs ? b2a::launch_prefill_pair(tq, tk, tv, p, static_cast<cudaStream_t>(stream))
+                       : b2a::launch_prefill(D, plan, tq, tk, tv, p, static_cast<cudaStream_t>(stream));
   if (rc == -3) return B2A_ERR_HEAD_DIM;
   return rc ? B2A_ERR_LAUNCH : B2A_OK;
 }

@@ -1,6 +1,8 @@
 // Kernel body of the tcgen05 causal GQA prefill; see prefill.cuh for the
 // design. The host-side launcher (tensor maps, argument checks) is at the end
 // of this file and is called from capi.cu.
+#include <cstdlib>
+
 #include "prefill.cuh"
 #include "softmax.cuh"
 
@@ -616,14 +618,27 @@ static int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const 
 // and 8192 head pairs ran 1-3 % slower (more KV heads in flight at once:
 // their K/V no longer fit in L2). Odd groups keep one-tile CTAs up to
 // kOneTileMaxRows (measured against row pairs: T=1024 +2-3 %, T=2048 -10 %).
+// Queries of at least this many rows (head dim 128, even GQA group) run on SM
+// pairs (prefill_pair.cu) when the environment variable B2A_PREFILL_SM_PAIRS
+// holds a positive row count; unset or 0 (the default): never. The SM-pair
+// kernel gives the same results bit for bit but measured slower (config 3:
+// 825 against 1065 TFLOP/s at T=8192), so it is opt-in.
+static int sm_pairs_min_rows() {
+  const char* s = std::getenv("B2A_PREFILL_SM_PAIRS");
+  if (!s || !*s) return 0;
+  const long v = std::strtol(s, nullptr, 10);
+  return v > 0 && v < (1L << 30) ? (int)v : 0;
+}
+
 PrefillPlan prefill_plan(int D, int Hq, int Hkv, int Tq, int Tk) {
-  (void)D;
   (void)Tk;
   const bool even_group = Hkv > 0 && Hq % Hkv == 0 && (Hq / Hkv) % 2 == 0;
+  const int pair_min = D == 128 && even_group ? sm_pairs_min_rows() : 0;
+  if (pair_min > 0 && Tq >= pair_min) return PrefillPlan{256, 2, 0, 1};
   if (kHeadPairs && even_group && Tq >= kHeadPairMinRows && Tq <= kHeadPairMaxRows)
-    return PrefillPlan{128, 2, 1};
-  if (Tq <= kOneTileMaxRows) return PrefillPlan{128, 1, 0};
-  return PrefillPlan{256, 2, 0};
+    return PrefillPlan{128, 2, 1, 0};
+  if (Tq <= kOneTileMaxRows) return PrefillPlan{128, 1, 0, 0};
+  return PrefillPlan{256, 2, 0, 0};
 }
 
 int launch_prefill(int D, const PrefillPlan& plan, const CUtensorMap& tq, const CUtensorMap& tk,

@@ -161,8 +161,14 @@ struct PrefillPlan {
   int rows_per_item;
   int tiles;       // query tiles per CTA (NQT)
   int head_pairs;
+  int sm_pairs;    // 1: fa_prefill_pair_kernel (prefill_pair.cu), D = 128
 };
 PrefillPlan prefill_plan(int D, int Hq, int Hkv, int Tq, int Tk);
+
+// Head dim 128 on SM pairs (prefill_pair.cu): cluster launch, 256 rows of two
+// query heads per item; K's tensor map has 32-row boxes, Q's and V's 128.
+int launch_prefill_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                        const PrefillParams& p, cudaStream_t st);
 
 // Launch the prefill kernel on `st` for the given plan.
 // Returns 0 on success, -3 for an unsupported head_dim, another negative
