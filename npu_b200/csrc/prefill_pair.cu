@@ -32,6 +32,17 @@
 // freed for the pair (tcgen05.alloc .cta_group::2, issued by warp 1 of both
 // CTAs). A cluster barrier after set-up and another before the free keep
 // either CTA's shared memory alive while the other can still reach it.
+// Limitation of the abort path (a wait past its bound, which sets the error
+// word): the peer CTA's K/V loads complete on the leader's barriers. So the
+// peer cannot wait for its own copies in flight before it leaves, as the
+// one-SM kernel's producer does. A late copy can then land in shared memory
+// that the SM has already given to a later CTA. The launch has failed by
+// then (the host reads the error word), and nothing leaves the SM's own
+// shared memory.
+//
+// Measured slower than the one-SM kernel (every half-block handoff waits for
+// both SMs). It is selected only when the caller sets B2A_PREFILL_SM_PAIRS
+// (prefill.cu, prefill_plan).
 #include "prefill.cuh"
 #include "softmax.cuh"
 
